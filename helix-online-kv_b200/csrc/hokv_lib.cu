@@ -1,0 +1,523 @@
+// hokv_lib.cu -- C ABI of the B200 compressed-KV hot path (declared in
+// include/hokv.h).  One translation unit: all kernels share the device status
+// flag below.  Host code validates arguments, picks template variants and
+// launches on the caller's stream; it allocates nothing.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "hokv_common.cuh"
+#include "cdc03.cuh"
+#include "codec.cuh"
+#include "dense.cuh"
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+namespace hokv {
+
+
+static thread_local std::string t_err;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return status;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return HOKV_OK;
+}
+
+static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+static inline bool is_pow2_in(int v, int lo, int hi) { return v >= lo && v <= hi && (v & (v - 1)) == 0; }
+static inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel), so
+// calls made later (e.g. inside CUDA-graph capture) issue no attribute change.
+template <typename K>
+static int ensure_smem(K kernel, size_t bytes) {
+  if (bytes <= 48 * 1024) return HOKV_OK;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return HOKV_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "cudaFuncSetAttribute(%zu B): %s", bytes, cudaGetErrorString(e));
+  done[key] = bytes;
+  return HOKV_OK;
+}
+
+template <int CS, int GT>
+static int launch_k6(const Cdc03P& p, cudaStream_t st) {
+  using Q = QGeo<CS, GT>;
+  const size_t regionA = std::max<size_t>((size_t)GT * CS * 1024, (size_t)GT * p.chunk * 2);
+  const size_t sm = Q::BYTES + regionA + (size_t)GT * 1024 + (size_t)GT * p.D * 4;
+  if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
+  dim3 grid((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
+  k6_candidates<CS, GT><<<grid, K6_THREADS, sm, st>>>(p);
+  return check_launch("k6_candidates");
+}
+
+static int dispatch_k6(const Cdc03P& p, cudaStream_t st) {
+#define HOKV_K6(cs_, gt_) if (p.CS == cs_ && p.GT == gt_) return launch_k6<cs_, gt_>(p, st);
+  HOKV_K6(4, 1) HOKV_K6(4, 2) HOKV_K6(4, 4) HOKV_K6(4, 8)
+  HOKV_K6(8, 1) HOKV_K6(8, 2) HOKV_K6(8, 4) HOKV_K6(8, 8)
+  HOKV_K6(16, 1) HOKV_K6(16, 2) HOKV_K6(16, 4) HOKV_K6(16, 8)
+  HOKV_K6(32, 1) HOKV_K6(32, 2) HOKV_K6(32, 4)
+#undef HOKV_K6
+  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: no K6 variant for code_bytes=%d group=%d", p.CS, p.GT);
+}
+
+template <int D, typename KVT>
+static int launch_k7(const Cdc03P& p, cudaStream_t st) {
+  const size_t sm = (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 + (size_t)(K7_THREADS / 32) * (D + 2) * 4 +
+                    (size_t)p.M * 1024;
+  if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
+  k7_select_attend<D, KVT><<<(unsigned)(p.B * p.Hkv * p.G), K7_THREADS, sm, st>>>(p);
+  return check_launch("k7_select_attend");
+}
+
+template <typename KVT>
+static int dispatch_k7_t(const Cdc03P& p, cudaStream_t st) {
+  switch (p.D) {
+    case 32: return launch_k7<32, KVT>(p, st);
+    case 64: return launch_k7<64, KVT>(p, st);
+    case 128: return launch_k7<128, KVT>(p, st);
+    case 256: return launch_k7<256, KVT>(p, st);
+  }
+  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: head_dim %d", p.D);
+}
+
+static int dispatch_k7(const Cdc03P& p, int kv_dtype, cudaStream_t st) {
+  if (kv_dtype == HOKV_BF16) return dispatch_k7_t<__nv_bfloat16>(p, st);
+  if (kv_dtype == HOKV_F16) return dispatch_k7_t<__half>(p, st);
+  if (kv_dtype == HOKV_F32) return dispatch_k7_t<float>(p, st);
+  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: head_dim %d", p.D);
+}
+
+}  // namespace hokv
+
+using namespace hokv;
+
+extern "C" {
+
+int hokv_abi_version(void) { return HOKV_ABI_VERSION; }
+
+const char* hokv_status_string(int s) {
+  switch (s) {
+    case HOKV_OK: return "ok";
+    case HOKV_ERR_INVALID: return "invalid argument";
+    case HOKV_ERR_UNSUPPORTED: return "unsupported configuration";
+    case HOKV_ERR_CUDA: return "CUDA error";
+    case HOKV_ERR_TIMEOUT: return "bounded device wait ran out";
+    case HOKV_ERR_DEVICE_INPUT: return "device found invalid input";
+    case HOKV_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown status";
+  }
+}
+
+const char* hokv_last_error(void) { return t_err.c_str(); }
+
+int hokv_dot_order_for(int64_t n_rows, int dim) { return dot_order_for(n_rows, dim); }
+
+int hokv_device_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(S(stream));
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "stream sync: %s", cudaGetErrorString(e));
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(int));
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_dev_status, &zero, sizeof(int));
+    return fail(v, "device reported: %s", hokv_status_string(v));
+  }
+  return HOKV_OK;
+}
+
+// ---------------------------------------------------------------- scalar ---
+int hokv_scalar_assign(const void* values, int dtype, int64_t n, int64_t values_stride, const float* centroids,
+                       int k, int64_t cent_stride, uint8_t* out, int64_t out_stride, int n_sets, void* stream) {
+  HOKV_REQUIRE(n >= 0 && n_sets >= 1, "scalar_assign: n=%lld n_sets=%d", (long long)n, n_sets);
+  HOKV_REQUIRE(k >= 1 && k <= 256, "scalar_assign: k=%d not in [1, 256]", k);
+  HOKV_REQUIRE(dtype == HOKV_F32 || dtype == HOKV_F16 || dtype == HOKV_BF16, "scalar_assign: dtype %d", dtype);
+  if (n == 0) return HOKV_OK;
+  HOKV_REQUIRE(values && centroids && out, "scalar_assign: null pointer");
+  dim3 grid((unsigned)std::min<int64_t>(cdiv(n, 256), 1024), (unsigned)n_sets);
+  k_scalar_assign<<<grid, 256, 0, S(stream)>>>(values, dtype, n, values_stride, centroids, k, cent_stride, out,
+                                               out_stride);
+  return check_launch("k_scalar_assign");
+}
+
+int hokv_scalar_decode(const uint8_t* idx, int64_t n, const float* centroids, int k, float* out, void* stream) {
+  HOKV_REQUIRE(n >= 0 && k >= 1 && k <= 256, "scalar_decode: n=%lld k=%d", (long long)n, k);
+  if (n == 0) return HOKV_OK;
+  k_scalar_decode<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 4096), 256, 0, S(stream)>>>(idx, n, centroids, k, out);
+  return check_launch("k_scalar_decode");
+}
+
+static size_t cub_sort_bytes(int64_t n) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortKeys(nullptr, bytes, (const float*)nullptr, (float*)nullptr, (int)n);
+  return bytes;
+}
+
+static inline size_t a256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t hokv_scalar_kmeans_workspace_size(int64_t n, int n_sets) {
+  return a256((size_t)n * n_sets * 4) + a256((size_t)n * n_sets) + a256((size_t)n * n_sets * 4) + a256(cub_sort_bytes(n));
+}
+
+int hokv_scalar_kmeans(const float* data, int64_t n, int64_t data_stride, int n_sets, int n_clusters, int max_iters,
+                       double rtol, float* centroids, int* k_out, int* iters_out, double* mse_out,
+                       uint8_t* assign_out, void* workspace, size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(n >= 1 && n < (1ll << 31), "scalar_kmeans: n=%lld", (long long)n);
+  HOKV_REQUIRE(n_sets >= 1 && n_clusters >= 1 && n_clusters <= 256, "scalar_kmeans: n_sets=%d n_clusters=%d", n_sets,
+               n_clusters);
+  HOKV_REQUIRE(max_iters >= 0, "scalar_kmeans: max_iters=%d", max_iters);
+  const size_t need = hokv_scalar_kmeans_workspace_size(n, n_sets);
+  if (!workspace || workspace_bytes < need)
+    return fail(HOKV_ERR_WORKSPACE, "scalar_kmeans: workspace %zu < %zu", workspace_bytes, need);
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  float* sorted = reinterpret_cast<float*>(w);
+  w += a256((size_t)n * n_sets * 4);
+  uint8_t* asg = w;
+  w += a256((size_t)n * n_sets);
+  float* mem = reinterpret_cast<float*>(w);
+  w += a256((size_t)n * n_sets * 4);
+  size_t tb = cub_sort_bytes(n);
+  for (int s = 0; s < n_sets; ++s) {
+    cudaError_t e = cub::DeviceRadixSort::SortKeys(w, tb, data + (int64_t)s * data_stride, sorted + (int64_t)s * n,
+                                                   (int)n, 0, 32, S(stream));
+    if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "scalar_kmeans sort: %s", cudaGetErrorString(e));
+  }
+  if (max_iters == 0) max_iters = 0;
+  k_scalar_kmeans<<<n_sets, 1024, 0, S(stream)>>>(data, n, data_stride, sorted, n_clusters, max_iters, rtol,
+                                                  centroids, k_out, iters_out, mse_out, asg, mem, assign_out);
+  return check_launch("k_scalar_kmeans");
+}
+
+size_t hokv_scalar_ema_workspace_size(int64_t n) { return a256((size_t)n) + a256((size_t)n * 4); }
+
+int hokv_scalar_ema(const float* values, int64_t n, float* centroids, int k, float alpha, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(n >= 1 && k >= 1 && k <= 256, "scalar_ema: n=%lld k=%d", (long long)n, k);
+  if (!workspace || workspace_bytes < hokv_scalar_ema_workspace_size(n))
+    return fail(HOKV_ERR_WORKSPACE, "scalar_ema: workspace too small");
+  uint8_t* asg = static_cast<uint8_t*>(workspace);
+  float* mem = reinterpret_cast<float*>(asg + a256((size_t)n));
+  k_scalar_ema<<<1, 1024, 0, S(stream)>>>(values, n, centroids, k, alpha, asg, mem);
+  return check_launch("k_scalar_ema");
+}
+
+int hokv_recon_stats(const float* x, const float* r, int64_t n, double* out4, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(n >= 1 && x && r && out4, "recon_stats: bad arguments");
+  if (!workspace || workspace_bytes < (size_t)n * 4) return fail(HOKV_ERR_WORKSPACE, "recon_stats: workspace");
+  float* tmp = static_cast<float*>(workspace);
+  k_recon_stats<<<1, 1024, 0, S(stream)>>>(x, r, n, tmp, out4);
+  return check_launch("k_recon_stats");
+}
+
+int hokv_scalar_vq_qkt(const float* q, const void* idx, int idx_dtype, int64_t seq_len, int head_dim,
+                       int64_t idx_stride, const float* codebook, int k, float scale, int accum_f64, float* scores,
+                       void* stream) {
+  HOKV_REQUIRE(seq_len >= 0 && head_dim >= 1 && head_dim <= 4096, "scalar_vq_qkt: seq_len=%lld head_dim=%d",
+               (long long)seq_len, head_dim);
+  HOKV_REQUIRE(k >= 1 && k <= 256, "scalar_vq_qkt: k=%d", k);
+  HOKV_REQUIRE(idx_dtype == HOKV_U8 || idx_dtype == HOKV_I32, "scalar_vq_qkt: idx dtype %d", idx_dtype);
+  if (seq_len == 0) return HOKV_OK;
+  const unsigned grid = (unsigned)cdiv(seq_len, 256);
+  const size_t sm = (size_t)head_dim * 4;
+  if (idx_dtype == HOKV_U8) {
+    if (accum_f64)
+      k_scalar_vq_qkt<uint8_t, double><<<grid, 256, sm, S(stream)>>>(q, (const uint8_t*)idx, seq_len, head_dim,
+                                                                      idx_stride, codebook, k, scale, scores);
+    else
+      k_scalar_vq_qkt<uint8_t, float><<<grid, 256, sm, S(stream)>>>(q, (const uint8_t*)idx, seq_len, head_dim,
+                                                                     idx_stride, codebook, k, scale, scores);
+  } else {
+    if (accum_f64)
+      k_scalar_vq_qkt<int32_t, double><<<grid, 256, sm, S(stream)>>>(q, (const int32_t*)idx, seq_len, head_dim,
+                                                                      idx_stride, codebook, k, scale, scores);
+    else
+      k_scalar_vq_qkt<int32_t, float><<<grid, 256, sm, S(stream)>>>(q, (const int32_t*)idx, seq_len, head_dim,
+                                                                     idx_stride, codebook, k, scale, scores);
+  }
+  return check_launch("k_scalar_vq_qkt");
+}
+
+// ------------------------------------------------------------ vector / PQ ---
+int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, int64_t x_set_stride, int M,
+                   int sub_dim, const float* cents, int cb_slots, int64_t cent_set_stride, const int* k,
+                   int64_t k_set_stride, uint8_t* out, int64_t out_row_stride, int64_t out_set_stride, int n_sets,
+                   int dot_order, void* stream) {
+  HOKV_REQUIRE(n >= 0 && M >= 1 && sub_dim >= 1 && n_sets >= 1, "pq_assign: n=%lld M=%d sub_dim=%d", (long long)n, M,
+               sub_dim);
+  HOKV_REQUIRE(cb_slots >= 1 && cb_slots <= 256, "pq_assign: cb_slots=%d", cb_slots);
+  HOKV_REQUIRE(dot_order >= 0 && dot_order <= 2, "pq_assign: dot_order=%d", dot_order);
+  HOKV_REQUIRE(x_dtype == HOKV_F32 || x_dtype == HOKV_F16 || x_dtype == HOKV_BF16, "pq_assign: dtype %d", x_dtype);
+  HOKV_REQUIRE(sub_dim <= 1024, "pq_assign: sub_dim %d > 1024", sub_dim);
+  if (n == 0) return HOKV_OK;
+  size_t sm = (256 + 8 * (size_t)sub_dim) * 4;
+  const size_t cb_sm = (size_t)cb_slots * (sub_dim + 1) * 4;
+  int use_smem = (sm + cb_sm) <= 160 * 1024;
+  if (use_smem) sm += cb_sm;
+  if (int st = ensure_smem(k_pq_assign, sm)) return st;
+  HOKV_REQUIRE(cdiv(n, 64) < (1ll << 31) && M <= 65535 && n_sets <= 65535, "pq_assign: grid too large");
+  dim3 grid((unsigned)cdiv(n, 64), (unsigned)M, (unsigned)n_sets);
+  k_pq_assign<<<grid, 256, sm, S(stream)>>>(x, x_dtype, n, x_row_stride, x_set_stride, M, sub_dim, cents, cb_slots,
+                                            cent_set_stride, k, k_set_stride, out, out_row_stride, out_set_stride,
+                                            dot_order, use_smem);
+  return check_launch("k_pq_assign");
+}
+
+int hokv_pq_decode(const uint8_t* codes, int64_t n, int64_t code_row_stride, int M, int sub_dim, const float* cents,
+                   int cb_slots, float* out, void* stream) {
+  HOKV_REQUIRE(n >= 0 && M >= 1 && sub_dim >= 1 && cb_slots >= 1 && cb_slots <= 256, "pq_decode: bad shape");
+  if (n == 0) return HOKV_OK;
+  const int64_t total = n * M * sub_dim;
+  k_pq_decode<<<(unsigned)std::min<int64_t>(cdiv(total, 256), 8192), 256, 0, S(stream)>>>(codes, n, code_row_stride,
+                                                                                           M, sub_dim, cents,
+                                                                                           cb_slots, out);
+  return check_launch("k_pq_decode");
+}
+
+static size_t vq_ws_per_set(int64_t n, int sd, int n_clusters) {
+  // asg, x2, mem (4 B each), keys (8 B, aligned), err (n*sd f32), Cn (k*sd f32)
+  size_t b = 12 * (size_t)n;
+  b += (8 - b % 8) % 8;
+  b += 8 * (size_t)n + 4 * (size_t)n * sd + 4 * (size_t)n_clusters * sd;
+  return a256(b);
+}
+
+size_t hokv_vq_kmeans_workspace_size(int64_t n, int sub_dim, int n_sets) {
+  return vq_ws_per_set(n, sub_dim, 256) * (size_t)n_sets;
+}
+
+int hokv_vq_kmeans(const float* data, int64_t n, int sub_dim, int64_t data_row_stride, int64_t data_set_stride,
+                   int n_sets, int n_clusters, int max_iters, double rtol, float* cents, int cb_slots, int* k_out,
+                   int* iters_out, double* mse_out, void* workspace, size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(n >= 1 && n <= 8192, "vq_kmeans: n=%lld not in [1, 8192]", (long long)n);
+  HOKV_REQUIRE(sub_dim >= 1 && n_sets >= 1, "vq_kmeans: sub_dim=%d n_sets=%d", sub_dim, n_sets);
+  HOKV_REQUIRE(n_clusters >= 1 && n_clusters <= 256 && cb_slots >= n_clusters && cb_slots <= 256,
+               "vq_kmeans: n_clusters=%d cb_slots=%d", n_clusters, cb_slots);
+  if ((int64_t)n_clusters * sub_dim > 32768)
+    return fail(HOKV_ERR_UNSUPPORTED, "vq_kmeans: n_clusters*sub_dim=%lld exceeds 32768",
+                (long long)n_clusters * sub_dim);
+  const size_t per = vq_ws_per_set(n, sub_dim, 256);
+  if (!workspace || workspace_bytes < per * (size_t)n_sets)
+    return fail(HOKV_ERR_WORKSPACE, "vq_kmeans: workspace %zu < %zu", workspace_bytes, per * (size_t)n_sets);
+  int npow = 1;
+  while (npow < n) npow <<= 1;
+  const size_t sm = (size_t)n_clusters * sub_dim * 4 * 2 + (size_t)n_clusters * 4 + (size_t)npow * 4;
+  if (int st = ensure_smem(k_vq_kmeans, sm)) return st;
+  k_vq_kmeans<<<n_sets, 1024, sm, S(stream)>>>(data, n, sub_dim, data_row_stride, data_set_stride, n_clusters,
+                                              max_iters, rtol, cents, cb_slots, k_out, iters_out, mse_out,
+                                              static_cast<unsigned char*>(workspace), (int64_t)per);
+  return check_launch("k_vq_kmeans");
+}
+
+int hokv_pq_tables(const float* q, int n_q, int M, int sub_dim, const float* cents, int cb_slots,
+                   int64_t cent_set_stride, const int* k, int64_t k_set_stride, const int* set_of_q, float* tables,
+                   int t_cols, void* stream) {
+  HOKV_REQUIRE(n_q >= 1 && M >= 1 && sub_dim >= 1 && t_cols >= 1, "pq_tables: bad shape");
+  HOKV_REQUIRE(cb_slots >= 1 && cb_slots <= 256 && M <= 65535, "pq_tables: cb_slots=%d M=%d", cb_slots, M);
+  dim3 grid((unsigned)n_q, (unsigned)M);
+  k_pq_tables<<<grid, 256, 0, S(stream)>>>(q, M, sub_dim, cents, cb_slots, cent_set_stride, k, k_set_stride, set_of_q,
+                                           tables, t_cols, DOT_GEMV);
+  return check_launch("k_pq_tables");
+}
+
+int hokv_pq_gather(const float* tables, int M, int t_cols, const uint8_t* codes, int64_t seq_len,
+                   int64_t code_row_stride, int apply_scale, float scale, float* scores, void* stream) {
+  HOKV_REQUIRE(M >= 1 && t_cols >= 1 && seq_len >= 0, "pq_gather: bad shape");
+  if (seq_len == 0) return HOKV_OK;
+  k_pq_gather<<<(unsigned)std::min<int64_t>(cdiv(seq_len, 256), 4096), 256, 0, S(stream)>>>(
+      tables, M, t_cols, codes, seq_len, code_row_stride, apply_scale, scale, scores);
+  return check_launch("k_pq_gather");
+}
+
+size_t hokv_pq_value_output_workspace_size(int M) { return (size_t)M * 256 * sizeof(double); }
+
+int hokv_pq_value_output(const double* weights, int64_t seq_len, const uint8_t* codes, int64_t code_row_stride, int M,
+                         int sub_dim, const float* cents, int cb_slots, const int* k, float* out, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(seq_len >= 0 && M >= 1 && sub_dim >= 1 && cb_slots >= 1 && cb_slots <= 256, "pq_value_output: shape");
+  if (!workspace || workspace_bytes < hokv_pq_value_output_workspace_size(M))
+    return fail(HOKV_ERR_WORKSPACE, "pq_value_output: workspace too small");
+  double* bins = static_cast<double*>(workspace);
+  cudaError_t e = cudaMemsetAsync(bins, 0, hokv_pq_value_output_workspace_size(M), S(stream));
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "pq_value_output memset: %s", cudaGetErrorString(e));
+  if (seq_len > 0)
+    k_value_bins<<<(unsigned)std::min<int64_t>(cdiv(seq_len * M, 256), 4096), 256, 0, S(stream)>>>(
+        weights, seq_len, codes, code_row_stride, M, bins);
+  k_value_out<<<M, 128, 0, S(stream)>>>(bins, M, sub_dim, cents, cb_slots, k, out);
+  return check_launch("k_value_out");
+}
+
+// ------------------------------------------------------------------ CDC-03 ---
+static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
+
+struct Plan {
+  int n_chunks, chunk, GT;
+  size_t cand_idx_bytes, cand_cnt_bytes;
+};
+
+static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
+  HOKV_REQUIRE(a, "cdc03: null args");
+  HOKV_REQUIRE(a->batch >= 1 && a->kv_heads >= 1, "cdc03: batch=%d kv_heads=%d", a->batch, a->kv_heads);
+  HOKV_REQUIRE(a->q_per_kv >= 1 && a->q_per_kv <= 8, "cdc03: q_per_kv=%d not in [1, 8]", a->q_per_kv);
+  HOKV_REQUIRE(a->head_dim == 32 || a->head_dim == 64 || a->head_dim == 128 || a->head_dim == 256,
+               "cdc03: head_dim=%d not in {32, 64, 128, 256}", a->head_dim);
+  HOKV_REQUIRE(a->n_subspaces >= 1, "cdc03: n_subspaces=%d", a->n_subspaces);
+  {
+    const int sd = a->sub_dim > 0 ? a->sub_dim : a->head_dim / a->n_subspaces;
+    HOKV_REQUIRE(sd >= 1 && a->n_subspaces * sd <= a->head_dim && (a->sub_dim > 0 || a->head_dim % a->n_subspaces == 0),
+                 "cdc03: M=%d x sub_dim=%d does not fit head_dim=%d", a->n_subspaces, sd, a->head_dim);
+  }
+  HOKV_REQUIRE(is_pow2_in(a->code_bytes, 4, 32) && a->n_subspaces <= a->code_bytes,
+               "cdc03: code_bytes=%d (M=%d)", a->code_bytes, a->n_subspaces);
+  HOKV_REQUIRE(a->cb_slots >= 1 && a->cb_slots <= 256, "cdc03: cb_slots=%d", a->cb_slots);
+  HOKV_REQUIRE(a->top_k >= 0 && a->sink_tokens >= 0 && a->hot_window >= 0, "cdc03: negative budget");
+  HOKV_REQUIRE(a->capacity >= 1 && a->capacity < (1ll << 30), "cdc03: capacity=%lld", (long long)a->capacity);
+  HOKV_REQUIRE(a->q && a->out && a->k && a->v && a->codes && a->codebook && a->cb_k && a->seq_len,
+               "cdc03: null pointer");
+  HOKV_REQUIRE(a->kv_dtype == HOKV_F16 || a->kv_dtype == HOKV_BF16 || a->kv_dtype == HOKV_F32,
+               "cdc03: kv dtype %d", a->kv_dtype);
+  HOKV_REQUIRE(a->q_dtype == HOKV_F32 || a->q_dtype == HOKV_F16 || a->q_dtype == HOKV_BF16, "cdc03: q dtype");
+  HOKV_REQUIRE(a->out_dtype == HOKV_F32 || a->out_dtype == HOKV_F16 || a->out_dtype == HOKV_BF16, "cdc03: out dtype");
+  HOKV_REQUIRE(aligned(a->codes, 16) && a->code_stride_b % 16 == 0 && a->code_stride_h % 16 == 0,
+               "cdc03: code store must be 16-byte aligned with 16-byte strides");
+  HOKV_REQUIRE(aligned(a->k, 16) && aligned(a->v, 16) && a->kv_stride_b % 8 == 0 && a->kv_stride_h % 8 == 0,
+               "cdc03: K/V stores must be 16-byte aligned with strides multiple of 8 elements");
+  const int64_t cold_cap = std::max<int64_t>(0, a->capacity - a->hot_window);
+  if (a->top_k > TOPK_MAX && a->top_k < cold_cap)
+    return fail(HOKV_ERR_UNSUPPORTED, "cdc03: top_k=%d > %d with a longer cold range", a->top_k, TOPK_MAX);
+  const int units = a->batch * a->kv_heads;
+  const int target = 296;  // two resident K6 CTAs per SM on 148 SMs
+  int nct = std::max(1, target / units);
+  int64_t chunk = cdiv(std::max<int64_t>(cold_cap, 1), nct);
+  chunk = cdiv(chunk, K6_THREADS) * K6_THREADS;
+  chunk = std::min<int64_t>(std::max<int64_t>(chunk, K6_THREADS), K6_CHUNK_MAX);
+  pl->chunk = (int)chunk;
+  pl->n_chunks = (int)std::max<int64_t>(1, cdiv(cold_cap, chunk));
+  pl->GT = gt_of(a->q_per_kv);
+  HOKV_REQUIRE(pl->GT * a->code_bytes <= 128, "cdc03: q_per_kv x code_bytes too large (%d x %d)", a->q_per_kv,
+               a->code_bytes);
+  pl->cand_idx_bytes = a256((size_t)units * pl->n_chunks * pl->GT * CAND_MAX * 4);
+  pl->cand_cnt_bytes = a256((size_t)units * pl->n_chunks * pl->GT * 4);
+  return HOKV_OK;
+}
+
+int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes) {
+  Plan pl;
+  if (int st = plan_cdc03(a, &pl)) return st;
+  *bytes = pl.cand_idx_bytes + pl.cand_cnt_bytes;
+  return HOKV_OK;
+}
+
+static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
+  Cdc03P p;
+  p.B = a->batch; p.Hkv = a->kv_heads; p.G = a->q_per_kv; p.D = a->head_dim; p.M = a->n_subspaces;
+  p.sd = a->sub_dim > 0 ? a->sub_dim : a->head_dim / a->n_subspaces; p.CS = a->code_bytes; p.slots = a->cb_slots; p.top_k = a->top_k;
+  p.sink = a->sink_tokens; p.hot = a->hot_window; p.scale = a->scale; p.lut_order = a->lut_order;
+  p.q = a->q; p.q_dtype = a->q_dtype; p.q_sb = a->q_stride_b;
+  p.out = a->out; p.out_dtype = a->out_dtype; p.out_sb = a->out_stride_b;
+  p.k = a->k; p.v = a->v; p.kv_sb = a->kv_stride_b; p.kv_sh = a->kv_stride_h; p.cap = a->capacity;
+  p.codes = a->codes; p.c_sb = a->code_stride_b; p.c_sh = a->code_stride_h;
+  p.cb = a->codebook; p.cb_sb = a->cb_stride_b; p.cb_sh = a->cb_stride_h;
+  p.cbk = a->cb_k; p.cbk_sb = a->cbk_stride_b; p.cbk_sh = a->cbk_stride_h;
+  p.seq_len = a->seq_len;
+  p.sel_idx = a->sel_idx; p.sel_score = a->sel_score; p.sel_count = a->sel_count;
+  unsigned char* w = static_cast<unsigned char*>(a->workspace);
+  p.cand_idx = reinterpret_cast<uint32_t*>(w);
+  p.cand_cnt = reinterpret_cast<int*>(w + pl.cand_idx_bytes);
+  p.n_chunks = pl.n_chunks; p.chunk = pl.chunk; p.GT = pl.GT;
+  return p;
+}
+
+static int cdc03_prepare(const hokv_cdc03_args* a, Cdc03P* p) {
+  Plan pl;
+  if (int st = plan_cdc03(a, &pl)) return st;
+  if (!a->workspace || a->workspace_bytes < pl.cand_idx_bytes + pl.cand_cnt_bytes)
+    return fail(HOKV_ERR_WORKSPACE, "cdc03: workspace %zu < %zu", a->workspace_bytes,
+                pl.cand_idx_bytes + pl.cand_cnt_bytes);
+  HOKV_REQUIRE(aligned(a->workspace, 16), "cdc03: workspace must be 16-byte aligned");
+  *p = make_params(a, pl);
+  return HOKV_OK;
+}
+
+int hokv_cdc03_candidates(const hokv_cdc03_args* a, void* stream) {
+  Cdc03P p;
+  if (int st = cdc03_prepare(a, &p)) return st;
+  return dispatch_k6(p, S(stream));
+}
+
+int hokv_cdc03_attend(const hokv_cdc03_args* a, void* stream) {
+  Cdc03P p;
+  if (int st = cdc03_prepare(a, &p)) return st;
+  return dispatch_k7(p, a->kv_dtype, S(stream));
+}
+
+int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream) {
+  Cdc03P p;
+  if (int st = cdc03_prepare(a, &p)) return st;
+  if (int st = dispatch_k6(p, S(stream))) return st;
+  return dispatch_k7(p, a->kv_dtype, S(stream));
+}
+
+int hokv_dense_attention(const float* q, const float* K, const float* V, int head_dim, int64_t seq_len, int mul_f64,
+                         double scale, int store_flags, const uint8_t* mask, void* scores, void* out, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  HOKV_REQUIRE(head_dim >= 1 && seq_len >= 1 && q && K && V && scores && out, "dense_attention: bad arguments");
+  if (!workspace || workspace_bytes < (size_t)seq_len * 8) return fail(HOKV_ERR_WORKSPACE, "dense_attention: workspace");
+  const int sf64 = store_flags & 1, of64 = (store_flags >> 1) & 1;
+  k_dense_scores<<<(unsigned)cdiv(seq_len * 32, 256), 256, 0, S(stream)>>>(q, K, head_dim, seq_len, scale, mul_f64, sf64,
+                                                                         mask, scores);
+  k_softmax<<<1, 1024, 0, S(stream)>>>(scores, sf64, seq_len, workspace);
+  k_weighted_sum<<<(unsigned)cdiv(head_dim, 128), 128, 0, S(stream)>>>(workspace, sf64, V, head_dim, seq_len, out, of64);
+  return check_launch("dense_attention");
+}
+
+int hokv_softmax(const void* in, int is_f64, int64_t n, void* out, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  (void)workspace; (void)workspace_bytes;
+  HOKV_REQUIRE(n >= 1 && in && out, "softmax: bad arguments");
+  k_softmax<<<1, 1024, 0, S(stream)>>>(in, is_f64, n, out);
+  return check_launch("k_softmax");
+}
+
+int hokv_prefilter_mask(const float* coarse, int k, const uint8_t* codes, int64_t seq_len, int top_p, uint8_t* mask,
+                        void* stream) {
+  HOKV_REQUIRE(k >= 1 && k <= 256 && seq_len >= 0 && top_p >= 0, "prefilter_mask: k=%d top_p=%d", k, top_p);
+  if (seq_len == 0) return HOKV_OK;
+  k_prefilter_mask<<<(unsigned)std::min<int64_t>(cdiv(seq_len, 256), 1024), 256, 0, S(stream)>>>(coarse, k, codes,
+                                                                                                  seq_len, top_p, mask);
+  return check_launch("k_prefilter_mask");
+}
+
+int hokv_scale_f32_to_f64(const float* in, int64_t n, double scale, double* out, void* stream) {
+  HOKV_REQUIRE(n >= 0 && (n == 0 || (in && out)), "scale_f32_to_f64: bad arguments");
+  if (n == 0) return HOKV_OK;
+  k_scale_f32_to_f64<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 4096), 256, 0, S(stream)>>>(in, n, scale, out);
+  return check_launch("k_scale_f32_to_f64");
+}
+
+int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* cold_to, int dot_order, void* stream) {
+  (void)a; (void)cold_from; (void)cold_to; (void)dot_order; (void)stream;
+  return fail(HOKV_ERR_UNSUPPORTED, "age_tokens: not built yet");
+}
+
+}  // extern "C"

@@ -1,0 +1,199 @@
+"""Batched CDC-03 decode attention on device-resident tiers.
+
+``CDC03Store`` holds, for B sequences x L layers x H_kv KV heads, the exact
+K/V store (fp16/bf16), the uint8 PQ codes of every token, the per-(sequence,
+layer, head) PQ codebooks and the per-sequence lengths, all in HBM:
+
+    k, v      [L, B, H_kv, capacity, D]           fp16 / bf16
+    codes     [L, B, H_kv, capacity, code_bytes]  uint8 (bytes >= M unused)
+    codebook  [L, B, H_kv, M, 256, D / M]         float32
+    cb_k      [L, B, H_kv, M]                     int32 (centroids per subspace)
+    seq_len   [B]                                 int32 (device)
+
+``decode`` runs one layer of CDC-03 attention (libhokv ``hokv_cdc03_decode``)
+for queries [B, H_q, D] on the current stream, with no host synchronisation,
+so a decode step over all layers can be captured in a CUDA graph.  The
+per-call selection rule is the reference's (compressed_attention.py:366-388)
+applied to the cold range [0, seq_len - hot_window); the hot window is always
+attended.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .product_codebook import SLOTS
+
+
+def code_bytes_for(M: int) -> int:
+    for c in (4, 8, 16, 32):
+        if M <= c:
+            return c
+    raise ValueError(f"at most 32 PQ subspaces are supported, got {M}")
+
+
+class CDC03Store:
+    def __init__(self, batch: int, n_layers: int, kv_heads: int, head_dim: int, capacity: int,
+                 n_subspaces: int = 8, dtype=torch.float16, device=None):
+        L.require_device()
+        if head_dim % n_subspaces:
+            raise ValueError(f"head_dim ({head_dim}) must be divisible by n_subspaces ({n_subspaces})")
+        self.B, self.L, self.H, self.D = batch, n_layers, kv_heads, head_dim
+        self.M = n_subspaces
+        self.sd = head_dim // n_subspaces
+        self.CS = code_bytes_for(n_subspaces)
+        self.cap = int(-(-capacity // 16) * 16)
+        dev = device or L.device()
+        self.k = torch.zeros((n_layers, batch, kv_heads, self.cap, head_dim), dtype=dtype, device=dev)
+        self.v = torch.zeros_like(self.k)
+        self.codes = torch.zeros((n_layers, batch, kv_heads, self.cap, self.CS), dtype=torch.uint8, device=dev)
+        self.codebook = torch.zeros((n_layers, batch, kv_heads, n_subspaces, SLOTS, self.sd), dtype=torch.float32,
+                                    device=dev)
+        self.cb_k = torch.zeros((n_layers, batch, kv_heads, n_subspaces), dtype=torch.int32, device=dev)
+        self.seq_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self._ws = None
+
+    # ---- calibration and assignment -----------------------------------------
+    def calibrate(self, layer: int, n_tokens: int = 128, sub_clusters: int = 256, max_iters: int = 30,
+                  rtol: float = 1e-4):
+        """Fit the PQ codebooks of one layer on tokens [0, n_tokens) of every (b, h)
+        (ProductCodebook.finalize_calibration, product_codebook.py:86-116)."""
+        n = int(n_tokens)
+        data = self.k[layer, :, :, :n, :].float().reshape(self.B * self.H, n, self.D).contiguous()
+        ws = L.workspace(L.lib().hokv_vq_kmeans_workspace_size(n, self.sd, self.M))
+        it = torch.zeros(self.M, dtype=torch.int32, device=data.device)
+        mse = torch.zeros(self.M, dtype=torch.float64, device=data.device)
+        cb = self.codebook[layer].reshape(self.B * self.H, self.M, SLOTS, self.sd)
+        kk = self.cb_k[layer].reshape(self.B * self.H, self.M)
+        for u in range(self.B * self.H):
+            L.check(L.lib().hokv_vq_kmeans(L.ptr(data[u]), n, self.sd, self.D, self.sd, self.M, sub_clusters,
+                                           max_iters, float(rtol), L.ptr(cb[u]), SLOTS, L.ptr(kk[u]), L.ptr(it),
+                                           L.ptr(mse), L.ptr(ws), ws.numel(), L.stream()), "vq_kmeans")
+
+    def assign(self, layer: int, start: int, end: int, order: int | None = None):
+        """PQ codes of tokens [start, end) of every (b, h) of one layer
+        (ProductCodebook.assign, product_codebook.py:118-145)."""
+        n = int(end) - int(start)
+        if n <= 0:
+            return
+        if order is None:
+            order = L.dot_order_for(n, self.sd)
+        for b in range(self.B):
+            x = self.k[layer, b, :, start:end, :]
+            out = self.codes[layer, b, :, start:end, :]
+            L.check(L.lib().hokv_pq_assign(L.ptr(x), L.dtype_code(x), n, self.D, self.cap * self.D, self.M, self.sd,
+                                           L.ptr(self.codebook[layer, b]), SLOTS, self.M * SLOTS * self.sd,
+                                           L.ptr(self.cb_k[layer, b]), self.M, L.ptr(out), self.CS,
+                                           self.cap * self.CS, self.H, order, L.stream()), "pq_assign")
+
+    # ---- decode ---------------------------------------------------------------
+    def args(self, layer: int, q, out, scale: float, top_k: int = 128, sink_tokens: int = 4,
+             hot_window: int = 256, sel_idx=None, sel_score=None, sel_count=None) -> L.Cdc03Args:
+        B, Hq, D = q.shape
+        if B != self.B or D != self.D or Hq % self.H:
+            raise ValueError(f"queries {tuple(q.shape)} do not match the store (B={self.B}, H_kv={self.H}, D={self.D})")
+        a = L.Cdc03Args()
+        a.batch, a.kv_heads, a.q_per_kv, a.head_dim = self.B, self.H, Hq // self.H, self.D
+        a.n_subspaces, a.sub_dim, a.code_bytes, a.cb_slots = self.M, self.sd, self.CS, SLOTS
+        a.top_k, a.sink_tokens, a.hot_window = int(top_k), int(sink_tokens), int(hot_window)
+        a.scale = float(np.float32(scale))
+        a.lut_order = L.DOT_GEMV
+        a.q, a.q_dtype, a.q_stride_b = q.data_ptr(), L.dtype_code(q), q.stride(0)
+        a.out, a.out_dtype, a.out_stride_b = out.data_ptr(), L.dtype_code(out), out.stride(0)
+        kl, vl = self.k[layer], self.v[layer]
+        a.k, a.v, a.kv_dtype = kl.data_ptr(), vl.data_ptr(), L.dtype_code(kl)
+        a.kv_stride_b, a.kv_stride_h = kl.stride(0), kl.stride(1)
+        a.capacity = self.cap
+        cl = self.codes[layer]
+        a.codes, a.code_stride_b, a.code_stride_h = cl.data_ptr(), cl.stride(0), cl.stride(1)
+        cb, ck = self.codebook[layer], self.cb_k[layer]
+        a.codebook, a.cb_stride_b, a.cb_stride_h = cb.data_ptr(), cb.stride(0), cb.stride(1)
+        a.cb_k, a.cbk_stride_b, a.cbk_stride_h = ck.data_ptr(), ck.stride(0), ck.stride(1)
+        a.seq_len = self.seq_len.data_ptr()
+        a.sel_idx = sel_idx.data_ptr() if sel_idx is not None else None
+        a.sel_score = sel_score.data_ptr() if sel_score is not None else None
+        a.sel_count = sel_count.data_ptr() if sel_count is not None else None
+        need = ctypes.c_size_t(0)
+        L.check(L.lib().hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need)), "cdc03_workspace_size")
+        if self._ws is None or self._ws.numel() < need.value:
+            self._ws = L.workspace(need.value)
+        a.workspace, a.workspace_bytes = self._ws.data_ptr(), self._ws.numel()
+        return a
+
+    def decode(self, layer: int, q, scale: float, top_k: int = 128, sink_tokens: int = 4, hot_window: int = 256,
+               out=None, out_dtype=None, return_selection: bool = False):
+        """CDC-03 attention of queries q [B, H_q, D] against one layer."""
+        q = q.contiguous()
+        if out is None:
+            out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=q.device)
+        sel = None
+        if return_selection:
+            B, Hq, _ = q.shape
+            cap = max(top_k, sink_tokens, 1)
+            sel = (torch.empty((B, Hq, cap), dtype=torch.int32, device=q.device),
+                   torch.empty((B, Hq, cap), dtype=torch.float32, device=q.device),
+                   torch.empty((B, Hq), dtype=torch.int32, device=q.device))
+        a = self.args(layer, q, out, scale, top_k, sink_tokens, hot_window, *(sel or (None, None, None)))
+        L.check(L.lib().hokv_cdc03_decode(ctypes.byref(a), L.stream()), "cdc03_decode")
+        return (out, sel) if return_selection else out
+
+
+def cdc03_single(q, K, V, codes, cents, k_counts, scale: float, top_k: int, sink_tokens: int, hot_window: int = 0,
+                 sub_dim: int | None = None):
+    """One query head against one key sequence, float32 K/V (the NumPy API path).
+
+    q [D], K/V [S, D] f32 CUDA; codes [S, M] uint8; cents [M, 256, sd]; k_counts [M].
+    Returns (out [D] f32, selected token indices, exact scores of those tokens).
+    """
+    S, D = K.shape
+    M = codes.shape[1]
+    sd = sub_dim or cents.shape[-1]
+    Dp = next(d for d in (32, 64, 128, 256, 1 << 30) if d >= D)
+    if Dp > 256:
+        raise ValueError(f"head_dim {D} > 256 is not supported by the CDC-03 kernels")
+    CS = code_bytes_for(M)
+    cap = int(-(-max(S, 1) // 16) * 16)
+    dev = K.device
+    Kp = torch.zeros((cap, Dp), dtype=torch.float32, device=dev)
+    Vp = torch.zeros_like(Kp)
+    Kp[:S, :D] = K
+    Vp[:S, :D] = V
+    qp = torch.zeros((1, 1, Dp), dtype=torch.float32, device=dev)
+    qp[0, 0, :D] = q
+    cp = torch.zeros((cap, CS), dtype=torch.uint8, device=dev)
+    cp[:S, :M] = codes
+    seq = torch.tensor([S], dtype=torch.int32, device=dev)
+    out = torch.empty((1, 1, Dp), dtype=torch.float32, device=dev)
+    kk = max(int(top_k), int(sink_tokens), 1)
+    sel_idx = torch.empty((1, 1, kk), dtype=torch.int32, device=dev)
+    sel_score = torch.empty((1, 1, kk), dtype=torch.float32, device=dev)
+    sel_count = torch.empty((1, 1), dtype=torch.int32, device=dev)
+    a = L.Cdc03Args()
+    a.batch = a.kv_heads = a.q_per_kv = 1
+    a.head_dim, a.n_subspaces, a.sub_dim, a.code_bytes, a.cb_slots = Dp, M, sd, CS, SLOTS
+    a.top_k, a.sink_tokens, a.hot_window = int(top_k), int(sink_tokens), int(hot_window)
+    a.scale = float(np.float32(scale))
+    a.lut_order = L.DOT_GEMV
+    a.q, a.q_dtype, a.q_stride_b = qp.data_ptr(), L.F32, Dp
+    a.out, a.out_dtype, a.out_stride_b = out.data_ptr(), L.F32, Dp
+    a.k, a.v, a.kv_dtype, a.kv_stride_b, a.kv_stride_h = Kp.data_ptr(), Vp.data_ptr(), L.F32, cap * Dp, cap * Dp
+    a.capacity = cap
+    a.codes, a.code_stride_b, a.code_stride_h = cp.data_ptr(), cap * CS, cap * CS
+    cents = cents.contiguous()
+    a.codebook, a.cb_stride_b, a.cb_stride_h = cents.data_ptr(), 0, 0
+    kc = k_counts.to(torch.int32).contiguous()
+    a.cb_k, a.cbk_stride_b, a.cbk_stride_h = kc.data_ptr(), 0, 0
+    a.seq_len = seq.data_ptr()
+    a.sel_idx, a.sel_score, a.sel_count = sel_idx.data_ptr(), sel_score.data_ptr(), sel_count.data_ptr()
+    need = ctypes.c_size_t(0)
+    L.check(L.lib().hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need)), "cdc03_workspace_size")
+    ws = L.workspace(need.value)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    L.check(L.lib().hokv_cdc03_decode(ctypes.byref(a), L.stream()), "cdc03_decode")
+    L.device_status()
+    n = int(sel_count[0, 0].item())
+    return out[0, 0, :D], sel_idx[0, 0, :n], sel_score[0, 0, :n]
