@@ -16,6 +16,7 @@
 // product_codebook.py:172-227 (tables, gather).
 #pragma once
 #include "hokv_common.cuh"
+#include <type_traits>
 
 namespace hokv {
 
@@ -25,6 +26,7 @@ constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
 constexpr int K7_CAP = 2048;         // key buffer of the exact selection
 constexpr int TOPK_MAX = 1024;       // largest top_k with k < S_c
+constexpr int MAX_CHUNKS = 512;      // K6 chunks per (sequence, KV head)
 
 struct Cdc03P {
   int B, Hkv, G, D, M, sd, CS, slots, top_k, sink, hot;
@@ -39,7 +41,7 @@ struct Cdc03P {
   const int* cbk; int64_t cbk_sb, cbk_sh;
   const int* seq_len;
   int* sel_idx; float* sel_score; int* sel_count;
-  uint32_t* cand_idx; int* cand_cnt;
+  uint32_t* cand_idx; int* cand_cnt; uint8_t* cand_code;
   int n_chunks, chunk, GT;
 };
 
@@ -118,29 +120,75 @@ __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
   for (int i = 0; i < W; ++i) w[i] = t[i];
 }
 
-// Sub-table values for one centroid row: T[g][s][j] = q_g[s-slice] . c  (BLAS order).
-template <int SD>
-__device__ __forceinline__ void lut_row(const float* __restrict__ sq, int D, const float* __restrict__ crow,
-                                        int s, int order, int GT, float* outv /*[GT]*/) {
-  float c[SD];
-#pragma unroll
-  for (int i = 0; i < SD; ++i) c[i] = __ldg(crow + i);
-  for (int g = 0; g < GT; ++g) outv[g] = dot_order(order, sq + g * D + s * SD, c, SD);
+template <int GT>
+__device__ __forceinline__ int approx_of(const uint32_t* acc, int g) {
+  // packing: acc[0] = h0 | h2 << 16, acc[1] = h1 | h3 << 16, acc[2] = h4 | h6 << 16, acc[3] = h5 | h7 << 16
+  if constexpr (GT == 1) return (int)acc[0];
+  else if constexpr (GT == 2) return (int)(g == 0 ? (acc[0] & 0xffffu) : (acc[0] >> 16));
+  else {
+    const uint32_t a = acc[(g >> 2) * 2 + (g & 1)];
+    return (int)((g & 2) ? (a >> 16) : (a & 0xffffu));
+  }
 }
 
-template <int CS, int GT>
+// ---- async copies and programmatic dependent launch ------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+// Let the next kernel in the stream start its independent prologue now.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+// Block until the previous kernel in the stream has completed and its writes are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Rows [0, lim) of every subspace of one (sequence, KV head) codebook are
+// staged in shared memory as stage[s][j][sd]; lim keeps the stage <= 64 KB.
+__device__ __forceinline__ int stage_rows(int slots, int D) {
+  const int lim = 16384 / D;  // D floats per (row of all subspaces) -> 64 KB
+  return slots < lim ? slots : lim;
+}
+
+__device__ __forceinline__ void stage_codebook(float* stage, const float* cb, int M, int slots, int sd, int lim,
+                                               int tid, int nthreads) {
+  // bytes per subspace block = lim * sd * 4 (multiple of 16 for sd % 4 == 0)
+  const int per_s = lim * sd / 4;  // 16-byte pieces per subspace
+  const int total = M * per_s;
+  for (int i = tid; i < total; i += nthreads) {
+    const int s = i / per_s, r = i - s * per_s;
+    cp_async16(stage + (int64_t)s * lim * sd + r * 4, cb + (int64_t)s * slots * sd + r * 4);
+  }
+}
+
+// Rotate W words so that out[i] = in[(i + r) % W] (r dynamic, W a power of two).
+template <int W, typename T>
+__device__ __forceinline__ void rotate_words(T (&w)[W], int r) {
+#pragma unroll
+  for (int bit = 1; bit < W; bit <<= 1) {
+    T t[W];
+    const bool on = (r & bit) != 0;
+#pragma unroll
+    for (int i = 0; i < W; ++i) t[i] = on ? w[(i + bit) % W] : w[i];
+#pragma unroll
+    for (int i = 0; i < W; ++i) w[i] = t[i];
+  }
+}
+
+template <int CS, int GT, int TPTM>
 __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   using Q = QGeo<CS, GT>;
+  static_assert(CS <= Q::COLS, "one row block");
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* qlut = smem;
-  float* T = reinterpret_cast<float*>(smem + Q::BYTES);            // [GT][CS][256] while building
-  uint16_t* apx = reinterpret_cast<uint16_t*>(smem + Q::BYTES);    // [GT][chunk] afterwards
-  const int regionA = max(GT * CS * 1024, GT * p.chunk * 2);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES + regionA);  // [GT][256]
-  float* sq = reinterpret_cast<float*>(smem + Q::BYTES + regionA + GT * 1024);  // [GT][D]
-  __shared__ float s_lo[GT * CS], s_hi[GT * CS], s_inv[GT];
-  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT];
+  unsigned char* qlut = smem;                                            // Q::BYTES
+  float* stage = reinterpret_cast<float*>(smem + Q::BYTES);              // codebook rows, then codes
+  const int stage_bytes = max(64 * 1024, p.chunk * CS);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES + stage_bytes);  // [GT][256]
+  float* sq = reinterpret_cast<float*>(hist + GT * 256);                 // [GT][D]
+  __shared__ unsigned s_lo[GT * CS], s_hi[GT * CS];
+  __shared__ float s_inv[GT], s_lof[GT * CS];
+  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_k[32];
 
+  pdl_launch_dependents();
   const int u = blockIdx.y, c = blockIdx.x;
   const int b = u / p.Hkv, h = u - b * p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -152,58 +200,43 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     return;
   }
   const int D = p.D, M = p.M, sd = p.sd;
+  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+  const int lim = stage_rows(p.slots, D);
+  const bool staged = (sd % 4) == 0;
 
-  // ---- queries of the GQA group -> shared f32 -----------------------------
+  // ---- prologue: stage the codebook, load queries and counts ----------------
+  if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K6_THREADS);
   for (int i = tid; i < GT * D; i += K6_THREADS) {
-    int g = i / D, d = i - g * D;
+    const int g = i / D, d = i - g * D;
     sq[i] = (g < p.G) ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
   }
-  for (int i = tid; i < GT * 256; i += K6_THREADS) hist[i] = 0;
-  if (tid < GT) s_cnt[tid] = 0;
-  __syncthreads();
-
-  // ---- exact sub-tables (fp32, BLAS order) into region A --------------------
-  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  const int* kbase = p.cbk + (int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh;
-  {
-    const int j = tid;  // K6_THREADS == 256 slots
-    float vals[GT];
-    for (int s = 0; s < M; ++s) {
-      int ks = kbase[s];
-      ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-      if (j < ks) {
-        const float* crow = cbase + ((int64_t)s * p.slots + j) * sd;
-        switch (sd) {
-          case 4: lut_row<4>(sq, D, crow, s, p.lut_order, GT, vals); break;
-          case 8: lut_row<8>(sq, D, crow, s, p.lut_order, GT, vals); break;
-          case 16: lut_row<16>(sq, D, crow, s, p.lut_order, GT, vals); break;
-          case 32: lut_row<32>(sq, D, crow, s, p.lut_order, GT, vals); break;
-          default:
-            for (int g = 0; g < GT; ++g) vals[g] = dot_order(p.lut_order, sq + g * D + s * sd, crow, sd);
-        }
-      } else {
-#pragma unroll
-        for (int g = 0; g < GT; ++g) vals[g] = 0.f;
-      }
-#pragma unroll
-      for (int g = 0; g < GT; ++g) T[(g * CS + s) * 256 + j] = vals[g];
-    }
+  if (tid < M) {
+    int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+    s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
   }
+  for (int i = tid; i < GT * 256; i += K6_THREADS) hist[i] = 0;
+  for (int i = tid; i < GT * CS; i += K6_THREADS) { s_lo[i] = 0xffffffffu; s_hi[i] = 0u; }
+  if (tid < GT) s_cnt[tid] = 0;
+  cp_async_wait_all();
   __syncthreads();
 
-  // ---- per (head, subspace) value range -----------------------------------
-  for (int pr = warp; pr < GT * M; pr += K6_THREADS / 32) {
-    const int g = pr / M, s = pr - g * M;
-    const float* row = T + (g * CS + s) * 256;
-    float mn = row[lane], mx = row[lane];
+  // exact sub-table value T[g][s][j] in the reference's BLAS order; j = tid
+  const int j = tid;
+  auto tval = [&](int g, int s) -> float {
+    if (j >= s_k[s]) return 0.f;
+    const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
+                                           : cbase + ((int64_t)s * p.slots + j) * sd;
+    return dot_order(p.lut_order, sq + g * D + s * sd, row, sd);
+  };
+
+  // ---- pass 1: per (head, subspace) value ranges -----------------------------
+  for (int s = 0; s < M; ++s) {
 #pragma unroll
-    for (int i = 1; i < 8; ++i) { float v = row[lane + 32 * i]; mn = fminf(mn, v); mx = fmaxf(mx, v); }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int g = 0; g < GT; ++g) {
+      const unsigned o = ord_f32(tval(g, s));
+      const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
+      if (lane == 0) { atomicMin(&s_lo[g * CS + s], mn); atomicMax(&s_hi[g * CS + s], mx); }
     }
-    if (lane == 0) { s_lo[g * CS + s] = mn; s_hi[g * CS + s] = mx; }
   }
   __syncthreads();
   if (tid < GT) {
@@ -211,7 +244,8 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     float rmax = 0.f;
     double sa = 0.0;
     for (int s = 0; s < M; ++s) {
-      float lo = s_lo[g * CS + s], hi = s_hi[g * CS + s];
+      const float lo = unord_f32(s_lo[g * CS + s]), hi = unord_f32(s_hi[g * CS + s]);
+      s_lof[g * CS + s] = lo;
       rmax = fmaxf(rmax, hi - lo);
       sa += fmax(fabs((double)lo), fabs((double)hi));
     }
@@ -226,118 +260,113 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   }
   __syncthreads();
 
-  // ---- quantised, replicated sub-tables -----------------------------------
+  // ---- pass 2: quantise and store the replicated 8-bit sub-tables -----------
   {
-    const int j = tid;
-    for (int rb = 0; rb < Q::RB; ++rb) {
-#pragma unroll 4
-      for (int i = 0; i < Q::COLS; ++i) {
-        const int col = (i + lane) & (Q::COLS - 1);
-        const int s = (CS <= Q::COLS) ? (col % CS) : (rb * Q::COLS + col);
-        uint32_t code[GT];
+    using EntT = typename std::conditional<Q::EW == 4, uint32_t, uint2>::type;
+    EntT w[CS];
 #pragma unroll
-        for (int g = 0; g < GT; ++g) {
-          uint32_t cv = 0;
-          if (s < M) {
-            float x = __fmul_rn(__fsub_rn(T[(g * CS + s) * 256 + j], s_lo[g * CS + s]), s_inv[g]);
-            x = fminf(fmaxf(rintf(x), 0.f), 255.f);
-            cv = (uint32_t)x;
-          }
-          code[g] = cv;
+    for (int s = 0; s < CS; ++s) {
+      uint32_t code[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        uint32_t cv = 0;
+        if (s < M) {
+          float x = __fmul_rn(__fsub_rn(tval(g, s), s_lof[g * CS + s]), s_inv[g]);
+          x = fminf(fmaxf(rintf(x), 0.f), 255.f);
+          cv = (uint32_t)x;
         }
-        const int e = (rb * 256 + j) * Q::COLS + col;
-        if constexpr (GT == 1) {
-          reinterpret_cast<uint32_t*>(qlut)[e] = code[0];
-        } else if constexpr (GT == 2) {
-          reinterpret_cast<uint32_t*>(qlut)[e] = code[0] | (code[1] << 16);
-        } else if constexpr (GT == 4) {
-          reinterpret_cast<uint32_t*>(qlut)[e] = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
-        } else {
-          uint2 v;
-          v.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
-          v.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
-          reinterpret_cast<uint2*>(qlut)[e] = v;
-        }
+        code[g] = cv;
+      }
+      if constexpr (GT == 1) w[s] = code[0];
+      else if constexpr (GT == 2) w[s] = code[0] | (code[1] << 16);
+      else if constexpr (GT == 4) w[s] = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
+      else {
+        uint2 v;
+        v.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
+        v.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
+        w[s] = v;
+      }
+    }
+    // lane L writes subspace (i + L) mod CS at step i: distinct columns per wavefront
+    rotate_words<CS>(w, lane % CS);
+    constexpr int NC = Q::COLS / CS;
+#pragma unroll
+    for (int cp = 0; cp < NC; ++cp) {
+      const int copy = (cp + (lane % Q::COLS) / CS) % NC;
+#pragma unroll
+      for (int i = 0; i < CS; ++i) {
+        const int col = copy * CS + ((i + lane) % CS);
+        reinterpret_cast<EntT*>(qlut)[j * Q::COLS + col] = w[i];
       }
     }
   }
-  __syncthreads();   // region A (T) is dead from here on; reused for apx
+  __syncthreads();  // codebook stage is dead: reuse it for the chunk's codes
 
-  // ---- stream the chunk's codes: 8-bit approximate scores ------------------
-  const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
+  // ---- stage the chunk's codes -------------------------------------------------
+  const int t0 = c * p.chunk;
+  const int ntok = min(p.chunk, cr.Sc - t0);
+  const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh + (int64_t)t0 * CS;
+  {
+    const int n16 = (ntok * CS + 15) / 16;
+    unsigned char* dst = reinterpret_cast<unsigned char*>(stage);
+    for (int i = tid; i < n16; i += K6_THREADS) cp_async16(dst + i * 16, gcodes + (int64_t)i * 16);
+    cp_async_wait_all();
+  }
+  __syncthreads();
+
+  // ---- 8-bit approximate scores, kept in registers ---------------------------
+  const unsigned char* scodes = reinterpret_cast<const unsigned char*>(stage);
   const int r = lane % CS;
   int colidx[CS];
 #pragma unroll
-  for (int uu = 0; uu < CS; ++uu) {
-    const int s = (uu + r) % CS;
-    colidx[uu] = Q::rb_of(s) * 256 * Q::COLS + Q::col_of(lane, s);
-  }
+  for (int uu = 0; uu < CS; ++uu) colidx[uu] = Q::col_of(lane, (uu + r) % CS);
+  uint32_t accs[TPTM][Q::NACC];
   int mxv[GT];
 #pragma unroll
   for (int g = 0; g < GT; ++g) mxv[g] = -1;
-  const int base = c * p.chunk;
   const int tpt = p.chunk / K6_THREADS;
-  constexpr int U = 4;
-  for (int it0 = 0; it0 < tpt; it0 += U) {
-    uint32_t w[U][Q::W];
-    bool valid[U];
 #pragma unroll
-    for (int q = 0; q < U; ++q) {
-      const int t = base + (it0 + q) * K6_THREADS + tid;
-      valid[q] = (it0 + q < tpt) && t >= lo_t && t < hi_t;
-      if (valid[q]) load_code<Q::W>(codes + (int64_t)t * CS, w[q]);
-      else {
+  for (int it = 0; it < TPTM; ++it) {
 #pragma unroll
-        for (int i = 0; i < Q::W; ++i) w[q][i] = 0;
+    for (int a = 0; a < Q::NACC; ++a) accs[it][a] = 0;
+    if (it >= tpt) continue;
+    const int lt = it * K6_THREADS + tid;
+    const int t = t0 + lt;
+    const bool valid = t >= lo_t && t < hi_t;
+    uint32_t w[Q::W];
+    if constexpr (Q::W == 1) w[0] = *reinterpret_cast<const uint32_t*>(scodes + lt * CS);
+    else if constexpr (Q::W == 2) { const uint2 v = *reinterpret_cast<const uint2*>(scodes + lt * CS); w[0] = v.x; w[1] = v.y; }
+    else {
+#pragma unroll
+      for (int q4 = 0; q4 < Q::W / 4; ++q4) {
+        const uint4 v = *reinterpret_cast<const uint4*>(scodes + lt * CS + q4 * 16);
+        w[q4 * 4 + 0] = v.x; w[q4 * 4 + 1] = v.y; w[q4 * 4 + 2] = v.z; w[q4 * 4 + 3] = v.w;
       }
     }
+    rotate_bytes<Q::W>(w, r);
 #pragma unroll
-    for (int q = 0; q < U; ++q) {
-      if (it0 + q >= tpt) break;
-      rotate_bytes<Q::W>(w[q], r);
-      uint32_t acc[Q::NACC];
-#pragma unroll
-      for (int a = 0; a < Q::NACC; ++a) acc[a] = 0;
-#pragma unroll
-      for (int uu = 0; uu < CS; ++uu) {
-        const uint32_t byte = (w[q][uu >> 2] >> (8 * (uu & 3))) & 0xffu;
-        const int e = colidx[uu] + (int)byte * Q::COLS;
-        if constexpr (Q::EW == 4) {
-          const uint32_t x = reinterpret_cast<const uint32_t*>(qlut)[e];
-          if constexpr (GT <= 2) {
-            acc[0] += x;
-          } else {
-            acc[0] += x & 0x00ff00ffu;
-            acc[1] += (x >> 8) & 0x00ff00ffu;
-          }
+    for (int uu = 0; uu < CS; ++uu) {
+      const uint32_t byte = (w[uu >> 2] >> (8 * (uu & 3))) & 0xffu;
+      const int e = colidx[uu] + (int)byte * Q::COLS;
+      if constexpr (Q::EW == 4) {
+        const uint32_t x = reinterpret_cast<const uint32_t*>(qlut)[e];
+        if constexpr (GT <= 2) {
+          accs[it][0] += x;
         } else {
-          const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
-          acc[0] += x.x & 0x00ff00ffu;
-          acc[1] += (x.x >> 8) & 0x00ff00ffu;
-          acc[2] += x.y & 0x00ff00ffu;
-          acc[3] += (x.y >> 8) & 0x00ff00ffu;
+          accs[it][0] += x & 0x00ff00ffu;
+          accs[it][1] += (x >> 8) & 0x00ff00ffu;
         }
-      }
-      int a[GT];
-      if constexpr (GT == 1) {
-        a[0] = (int)acc[0];
-      } else if constexpr (GT == 2) {
-        a[0] = (int)(acc[0] & 0xffffu); a[1] = (int)(acc[0] >> 16);
       } else {
-        // acc[0] = h0 | h2<<16, acc[1] = h1 | h3<<16 (, acc[2] = h4 | h6<<16, acc[3] = h5 | h7<<16)
-        a[0] = (int)(acc[0] & 0xffffu); a[2] = (int)(acc[0] >> 16);
-        a[1] = (int)(acc[1] & 0xffffu); a[3] = (int)(acc[1] >> 16);
-        if constexpr (GT == 8) {
-          a[4] = (int)(acc[2] & 0xffffu); a[6] = (int)(acc[2] >> 16);
-          a[5] = (int)(acc[3] & 0xffffu); a[7] = (int)(acc[3] >> 16);
-        }
+        const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
+        accs[it][0] += x.x & 0x00ff00ffu;
+        accs[it][1] += (x.x >> 8) & 0x00ff00ffu;
+        accs[it][2] += x.y & 0x00ff00ffu;
+        accs[it][3] += (x.y >> 8) & 0x00ff00ffu;
       }
-      const int lt = (it0 + q) * K6_THREADS + tid;
+    }
+    if (valid) {
 #pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        apx[g * p.chunk + lt] = (uint16_t)a[g];
-        if (valid[q]) mxv[g] = max(mxv[g], a[g]);
-      }
+      for (int g = 0; g < GT; ++g) mxv[g] = max(mxv[g], approx_of<GT>(accs[it], g));
     }
   }
 
@@ -354,10 +383,10 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     uint32_t ls = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) ls += hg[lane * 8 + i];
-    uint32_t suf = ls;  // inclusive suffix over lanes >= lane
+    uint32_t suf = ls;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+      const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
       if (lane + o < 32) suf += t;
     }
     const uint32_t kp = (uint32_t)cr.kp;
@@ -381,14 +410,20 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   }
   __syncthreads();
 
-  // ---- emit candidates ------------------------------------------------------
-  uint32_t* cand = p.cand_idx + ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
-  for (int it = 0; it < tpt; ++it) {
-    const int t = base + it * K6_THREADS + tid;
-    const bool valid = t >= lo_t && t < hi_t;
+  // ---- emit candidates: token index and its code row --------------------------
+  const int64_t cbase_idx = ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
+  uint32_t* cand = p.cand_idx + cbase_idx;
+  uint8_t* ccode = p.cand_code + cbase_idx * CS;
+#pragma unroll
+  for (int it = 0; it < TPTM; ++it) {
+    if (it >= tpt) break;
     const int lt = it * K6_THREADS + tid;
-    for (int g = 0; g < p.G; ++g) {
-      const bool pred = valid && ((int)apx[g * p.chunk + lt] >= s_thr[g]);
+    const int t = t0 + lt;
+    const bool valid = t >= lo_t && t < hi_t;
+#pragma unroll
+    for (int g = 0; g < GT; ++g) {
+      if (g >= p.G) break;   // uniform across the block
+      const bool pred = valid && approx_of<GT>(accs[it], g) >= s_thr[g];
       const unsigned m = __ballot_sync(0xffffffffu, pred);
       if (m) {
         const int leader = __ffs(m) - 1;
@@ -396,7 +431,13 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
         if (lane == leader) basep = atomicAdd(&s_cnt[g], __popc(m));
         basep = __shfl_sync(0xffffffffu, basep, leader);
         const int slot = basep + __popc(m & ((1u << lane) - 1u));
-        if (pred && slot < CAND_MAX) cand[g * CAND_MAX + slot] = (uint32_t)t;
+        if (pred && slot < CAND_MAX) {
+          cand[g * CAND_MAX + slot] = (uint32_t)t;
+          uint8_t* dst = ccode + ((int64_t)g * CAND_MAX + slot) * CS;
+#pragma unroll
+          for (int q4 = 0; q4 < CS; q4 += 4)
+            *reinterpret_cast<uint32_t*>(dst + q4) = *reinterpret_cast<const uint32_t*>(scodes + lt * CS + q4);
+        }
       }
     }
   }
@@ -529,15 +570,17 @@ template <int D, typename KVT>
 __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   using A = AttnGeo<D>;
   constexpr int NW = K7_THREADS / 32;
-  constexpr int U = 4;
+  constexpr int U = 8;
   extern __shared__ __align__(16) unsigned char smem[];
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem);                        // [K7_CAP]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + K7_CAP * 8);           // [1024]
-  int* sel = reinterpret_cast<int*>(smem + K7_CAP * 8 + 4096);               // [TOPK_MAX]
-  float* part = reinterpret_cast<float*>(smem + K7_CAP * 8 + 4096 + TOPK_MAX * 4);  // [NW][D + 2]
-  float* T = part + NW * (D + 2);                                            // [M][256]
+  float* T = reinterpret_cast<float*>(smem);                                 // [M][256] exact sub-table
+  unsigned char* X = smem + p.M * 1024;                                      // prologue: codebook stage;
+  float* stage = reinterpret_cast<float*>(X);                                // afterwards the buffers below
+  uint64_t* keys = reinterpret_cast<uint64_t*>(X);                           // [K7_CAP]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(X + K7_CAP * 8);              // [1024]
+  int* sel = reinterpret_cast<int*>(X + K7_CAP * 8 + 4096);                  // [TOPK_MAX]
+  float* part = reinterpret_cast<float*>(X + K7_CAP * 8 + 4096 + TOPK_MAX * 4);  // [NW][D + 2]
   __shared__ float s_q[D];
-  __shared__ int s_n;
+  __shared__ int s_n, s_k[32], s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
   __shared__ SelShared s_sel;
 
   const int Hq = p.Hkv * p.G;
@@ -546,13 +589,41 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int hq = h * p.G + g;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ColdRange cr = cold_range(p, b);
+  const bool topk_mode = !(cr.k >= cr.Sc) && cr.kp > 0;
 
+  // ---- prologue (independent of the candidate stage): q, exact sub-table ----
   for (int d = tid; d < D; d += K7_THREADS)
     s_q[d] = load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)hq * D + d);
   if (tid == 0) s_n = 0;
+  const int M = p.M, sd = p.sd;
+  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+  const int lim = stage_rows(p.slots, p.M * sd);
+  const bool staged = (sd % 4) == 0;
+  if (topk_mode) {
+    if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K7_THREADS);
+    if (tid < M) {
+      int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+      s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
+    }
+    cp_async_wait_all();
+  }
+  __syncthreads();
+  if (topk_mode) {
+    for (int i = tid; i < M * 256; i += K7_THREADS) {
+      const int s = i >> 8, j = i & 255;
+      float t = 0.f;
+      if (j < s_k[s]) {
+        const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
+                                               : cbase + ((int64_t)s * p.slots + j) * sd;
+        t = dot_order(p.lut_order, s_q + s * sd, row, sd);
+      }
+      T[i] = t;
+    }
+  }
+  // ---- wait for the candidate stage ------------------------------------------
+  pdl_wait();
   __syncthreads();
 
-  // ---- which cold tokens are attended --------------------------------------
   int n_sel;
   bool explicit_sel = false;
   if (cr.k >= cr.Sc) {
@@ -561,39 +632,60 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     n_sel = cr.sink;
   } else {
     explicit_sel = true;
-    const int M = p.M, sd = p.sd;
-    const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-    const int* kbase = p.cbk + (int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh;
-    for (int i = tid; i < M * 256; i += K7_THREADS) {
-      const int s = i >> 8, j = i & 255;
-      int ks = kbase[s];
-      ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-      T[i] = (j < ks) ? dot_order(p.lut_order, s_q + s * sd, cbase + ((int64_t)s * p.slots + j) * sd, sd) : 0.f;
+    const float scale = p.scale;
+    const int64_t cbase_idx = (int64_t)u * p.n_chunks * p.GT;
+    // candidate counts of every chunk (-1: list overflowed, rescan the chunk)
+    for (int c = tid; c < p.n_chunks; c += K7_THREADS) s_cnt[c] = p.cand_cnt[cbase_idx + (int64_t)c * p.GT + g];
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int c = 0; c < p.n_chunks; ++c) { s_off[c] = acc; acc += s_cnt[c] > 0 ? s_cnt[c] : 0; }
+      s_off[p.n_chunks] = acc;
     }
     __syncthreads();
+    const int n_listed = s_off[p.n_chunks];
+    // listed candidates: index + code row written by the candidate stage
+    for (int base = 0; base < n_listed; base += K7_THREADS) {
+      if (s_n + K7_THREADS > K7_CAP) {
+        select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
+        if (tid == 0) s_n = min(s_n, cr.kp);
+        __syncthreads();
+      }
+      const int i = base + tid;
+      if (i < n_listed) {
+        int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= i < s_off[c + 1]
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_off[mid] <= i) lo = mid; else hi = mid - 1;
+        }
+        const int c = lo;
+        const int slot = i - s_off[c];
+        const int64_t e = (cbase_idx + (int64_t)c * p.GT + g) * CAND_MAX + slot;
+        const uint32_t t = p.cand_idx[e];
+        const uint8_t* row = p.cand_code + e * p.CS;
+        float sum = 0.f;
+        for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + row[s]]);
+        keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), t);
+      }
+      __syncthreads();
+    }
+    // overflowed chunks: rescan every non-sink token of the chunk
     const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
-    const float scale = p.scale;
     for (int c = 0; c < p.n_chunks; ++c) {
+      if (s_cnt[c] >= 0) continue;
       const int clo = max(c * p.chunk, cr.sink), chi = min((c + 1) * p.chunk, cr.Sc);
-      if (clo >= chi) continue;
-      const int cnt = p.cand_cnt[((int64_t)u * p.n_chunks + c) * p.GT + g];
-      const uint32_t* cl = p.cand_idx + (((int64_t)u * p.n_chunks + c) * p.GT + g) * CAND_MAX;
-      const int ntok = (cnt >= 0) ? min(cnt, CAND_MAX) : (chi - clo);
-      for (int base = 0; base < ntok; base += K7_THREADS) {
+      for (int base = clo; base < chi; base += K7_THREADS) {
         if (s_n + K7_THREADS > K7_CAP) {
           select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
           if (tid == 0) s_n = min(s_n, cr.kp);
           __syncthreads();
         }
-        const int i = base + tid;
-        if (i < ntok) {
-          const int t = (cnt >= 0) ? (int)cl[i] : clo + i;
+        const int t = base + tid;
+        if (t < chi) {
           const uint8_t* row = codes + (int64_t)t * p.CS;
           float sum = 0.f;
           for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + row[s]]);
-          const float sc = fmul(sum, scale);
-          const int slot = atomicAdd(&s_n, 1);
-          keys[slot] = sel_key(sc, (uint32_t)t);
+          keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), (uint32_t)t);
         }
         __syncthreads();
       }

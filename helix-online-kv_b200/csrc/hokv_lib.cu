@@ -62,11 +62,14 @@ static int ensure_smem(K kernel, size_t bytes) {
 template <int CS, int GT>
 static int launch_k6(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
-  const size_t regionA = std::max<size_t>((size_t)GT * CS * 1024, (size_t)GT * p.chunk * 2);
-  const size_t sm = Q::BYTES + regionA + (size_t)GT * 1024 + (size_t)GT * p.D * 4;
-  if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
+  constexpr int TPTM = GT == 8 ? 8 : 16;
+  if (p.chunk > TPTM * K6_THREADS || (size_t)p.chunk * CS > 64 * 1024)
+    return fail(HOKV_ERR_INVALID, "cdc03: chunk %d too large for this variant", p.chunk);
+  const size_t stage = std::max<size_t>(64 * 1024, (size_t)p.chunk * CS);
+  const size_t sm = Q::BYTES + stage + (size_t)GT * 1024 + (size_t)GT * p.D * 4;
+  if (int e = ensure_smem(k6_candidates<CS, GT, TPTM>, sm)) return e;
   dim3 grid((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
-  k6_candidates<CS, GT><<<grid, K6_THREADS, sm, st>>>(p);
+  k6_candidates<CS, GT, TPTM><<<grid, K6_THREADS, sm, st>>>(p);
   return check_launch("k6_candidates");
 }
 
@@ -80,12 +83,28 @@ static int dispatch_k6(const Cdc03P& p, cudaStream_t st) {
   return fail(HOKV_ERR_UNSUPPORTED, "cdc03: no K6 variant for code_bytes=%d group=%d", p.CS, p.GT);
 }
 
+// K7 is launched with programmatic stream serialization: its prologue (query,
+// codebook stage, exact sub-table) overlaps the tail of K6, and it blocks in
+// griddepcontrol.wait before reading K6's candidate lists.
 template <int D, typename KVT>
 static int launch_k7(const Cdc03P& p, cudaStream_t st) {
-  const size_t sm = (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 + (size_t)(K7_THREADS / 32) * (D + 2) * 4 +
-                    (size_t)p.M * 1024;
+  const int lim = std::min(p.slots, 16384 / (p.M * p.sd));
+  const size_t stage = (size_t)p.M * lim * p.sd * 4;
+  const size_t bufs = (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 + (size_t)(K7_THREADS / 32) * (D + 2) * 4;
+  const size_t sm = (size_t)p.M * 1024 + std::max(stage, bufs);
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
-  k7_select_attend<D, KVT><<<(unsigned)(p.B * p.Hkv * p.G), K7_THREADS, sm, st>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.B * p.Hkv * p.G));
+  cfg.blockDim = dim3(K7_THREADS);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k7_select_attend<D, KVT>, p);
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "k7_select_attend launch: %s", cudaGetErrorString(e));
   return check_launch("k7_select_attend");
 }
 
@@ -372,7 +391,7 @@ static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct Plan {
   int n_chunks, chunk, GT;
-  size_t cand_idx_bytes, cand_cnt_bytes;
+  size_t cand_idx_bytes, cand_cnt_bytes, cand_code_bytes;
 };
 
 static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
@@ -406,25 +425,30 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
   if (a->top_k > TOPK_MAX && a->top_k < cold_cap)
     return fail(HOKV_ERR_UNSUPPORTED, "cdc03: top_k=%d > %d with a longer cold range", a->top_k, TOPK_MAX);
   const int units = a->batch * a->kv_heads;
+  pl->GT = gt_of(a->q_per_kv);
+  HOKV_REQUIRE(!(pl->GT == 8 && a->code_bytes > 16), "cdc03: q_per_kv > 4 needs code_bytes <= 16");
+  const int64_t chunk_max = std::min<int64_t>(pl->GT == 8 ? 2048 : K6_CHUNK_MAX, 65536 / a->code_bytes);
   const int target = 296;  // two resident K6 CTAs per SM on 148 SMs
   int nct = std::max(1, target / units);
   int64_t chunk = cdiv(std::max<int64_t>(cold_cap, 1), nct);
   chunk = cdiv(chunk, K6_THREADS) * K6_THREADS;
-  chunk = std::min<int64_t>(std::max<int64_t>(chunk, K6_THREADS), K6_CHUNK_MAX);
+  chunk = std::min<int64_t>(std::max<int64_t>(chunk, K6_THREADS), chunk_max);
   pl->chunk = (int)chunk;
   pl->n_chunks = (int)std::max<int64_t>(1, cdiv(cold_cap, chunk));
-  pl->GT = gt_of(a->q_per_kv);
-  HOKV_REQUIRE(pl->GT * a->code_bytes <= 128, "cdc03: q_per_kv x code_bytes too large (%d x %d)", a->q_per_kv,
-               a->code_bytes);
-  pl->cand_idx_bytes = a256((size_t)units * pl->n_chunks * pl->GT * CAND_MAX * 4);
+  if (pl->n_chunks > MAX_CHUNKS)
+    return fail(HOKV_ERR_UNSUPPORTED, "cdc03: capacity %lld needs %d chunks > %d", (long long)a->capacity,
+                pl->n_chunks, MAX_CHUNKS);
+  const size_t slots = (size_t)units * pl->n_chunks * pl->GT * CAND_MAX;
+  pl->cand_idx_bytes = a256(slots * 4);
   pl->cand_cnt_bytes = a256((size_t)units * pl->n_chunks * pl->GT * 4);
+  pl->cand_code_bytes = a256(slots * a->code_bytes);
   return HOKV_OK;
 }
 
 int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes) {
   Plan pl;
   if (int st = plan_cdc03(a, &pl)) return st;
-  *bytes = pl.cand_idx_bytes + pl.cand_cnt_bytes;
+  *bytes = pl.cand_idx_bytes + pl.cand_cnt_bytes + pl.cand_code_bytes;
   return HOKV_OK;
 }
 
@@ -444,6 +468,7 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   unsigned char* w = static_cast<unsigned char*>(a->workspace);
   p.cand_idx = reinterpret_cast<uint32_t*>(w);
   p.cand_cnt = reinterpret_cast<int*>(w + pl.cand_idx_bytes);
+  p.cand_code = w + pl.cand_idx_bytes + pl.cand_cnt_bytes;
   p.n_chunks = pl.n_chunks; p.chunk = pl.chunk; p.GT = pl.GT;
   return p;
 }
@@ -451,9 +476,9 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
 static int cdc03_prepare(const hokv_cdc03_args* a, Cdc03P* p) {
   Plan pl;
   if (int st = plan_cdc03(a, &pl)) return st;
-  if (!a->workspace || a->workspace_bytes < pl.cand_idx_bytes + pl.cand_cnt_bytes)
-    return fail(HOKV_ERR_WORKSPACE, "cdc03: workspace %zu < %zu", a->workspace_bytes,
-                pl.cand_idx_bytes + pl.cand_cnt_bytes);
+  const size_t need = pl.cand_idx_bytes + pl.cand_cnt_bytes + pl.cand_code_bytes;
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(HOKV_ERR_WORKSPACE, "cdc03: workspace %zu < %zu", a->workspace_bytes, need);
   HOKV_REQUIRE(aligned(a->workspace, 16), "cdc03: workspace must be 16-byte aligned");
   *p = make_params(a, pl);
   return HOKV_OK;
