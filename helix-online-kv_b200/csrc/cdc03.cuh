@@ -1,16 +1,21 @@
 // cdc03.cuh -- PQ lookup tables, ADC scoring and CDC-03 decode attention.
 //
-// Decode step, per layer:
-//   K6 k6_candidates  grid (chunks, B*H_kv): builds the per-KV-head sub-tables
-//      for the G query heads of the GQA group, quantises them to 8-bit entries
-//      in a bank-conflict-free shared-memory layout, streams the uint8 PQ codes
-//      of one chunk of cold tokens, and emits the token indices whose 8-bit
-//      score lies within the proven error band of the chunk's top-k boundary.
-//   K7 k7_select_attend  grid (B*H_kv*G): rebuilds the exact fp32 sub-table of
-//      one query head, rescores the candidates in the reference's summation
-//      order, selects sinks + top-(k - sinks) exactly (ties to the lower index)
-//      and runs exact softmax attention over the selected cold tokens plus the
-//      hot window, gathering fp16/bf16 K/V rows straight into registers.
+// Decode step, per layer, three kernels chained with programmatic dependent
+// launch (each starts its independent prologue while the previous one runs):
+//   K5 k5_tables    grid (B*H_kv): per (sequence, KV head), the exact fp32
+//      sub-tables T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads of
+//      the GQA group (BLAS order), and their quantised image: codes of
+//      floor(65535 / M) levels packed in 16-bit lanes, laid out so that every
+//      shared-memory lookup of K6 is bank-conflict free.
+//   K6 k6_candidates  grid (chunks, B*H_kv): streams the uint8 PQ codes of one
+//      chunk of cold tokens (prefetched while K5 runs), sums quantised table
+//      entries per token in integer lanes, finds a lower bound of the chunk's
+//      k'-th largest approximate score and emits every token whose score lies
+//      within the proven error band of it (index + code row).
+//   K7 k7_select_attend  grid (B*H_kv*G): attends the hot window before it
+//      waits for K6, then rescores the candidates exactly in the reference's
+//      summation order, selects sinks + top-(k - sinks) (ties to the lower
+//      token index) and finishes softmax attention over them.
 //
 // Reference: helix_online_kv/compressed_attention.py:315-412 (hybrid_pq_attention),
 // product_codebook.py:172-227 (tables, gather).
@@ -20,6 +25,7 @@
 
 namespace hokv {
 
+constexpr int K5_THREADS = 512;
 constexpr int K6_THREADS = 256;
 constexpr int K6_CHUNK_MAX = 4096;   // tokens per K6 CTA (16 per thread)
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
@@ -27,6 +33,7 @@ constexpr int K7_THREADS = 256;
 constexpr int K7_CAP = 2048;         // key buffer of the exact selection
 constexpr int TOPK_MAX = 1024;       // largest top_k with k < S_c
 constexpr int MAX_CHUNKS = 512;      // K6 chunks per (sequence, KV head)
+constexpr int REFINE_BINS = 512;
 
 struct Cdc03P {
   int B, Hkv, G, D, M, sd, CS, slots, top_k, sink, hot;
@@ -41,11 +48,15 @@ struct Cdc03P {
   const int* cbk; int64_t cbk_sb, cbk_sh;
   const int* seq_len;
   int* sel_idx; float* sel_score; int* sel_count;
+  // workspace
   uint32_t* cand_idx; int* cand_cnt; uint8_t* cand_code;
-  int n_chunks, chunk, GT;
+  unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (K5 -> K6)
+  float* texact;          // [units][GT][CS][256]    exact sub-tables (K5 -> K7)
+  int* margin;            // [units][GT]             error band in code units (K5 -> K6)
+  int n_chunks, chunk, GT, qimg_bytes;
 };
 
-// Per-sequence geometry of the cold range, identical in K6 and K7.
+// Per-sequence geometry of the cold range, identical in all three kernels.
 struct ColdRange {
   int S, Sc, k, sink, kp;
 };
@@ -61,42 +72,67 @@ __device__ __forceinline__ ColdRange cold_range(const Cdc03P& p, int b) {
   return r;
 }
 
+// ---- async copies and programmatic dependent launch ------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+// Let the next kernel in the stream start its independent prologue now.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+// Block until the previous kernel in the stream has completed and its writes are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Rows [0, lim) of every subspace of one (sequence, KV head) codebook are
+// staged in shared memory as stage[s][j][sd]; lim keeps the stage <= 64 KB.
+__host__ __device__ __forceinline__ int stage_rows(int slots, int covered_dims) {
+  const int lim = 16384 / covered_dims;
+  return slots < lim ? slots : lim;
+}
+
+__device__ __forceinline__ void stage_codebook(float* stage, const float* cb, int M, int slots, int sd, int lim,
+                                               int tid, int nthreads) {
+  const int per_s = lim * sd / 4;  // 16-byte pieces per subspace (sd % 4 == 0)
+  const int total = M * per_s;
+  for (int i = tid; i < total; i += nthreads) {
+    const int s = i / per_s, r = i - s * per_s;
+    cp_async16(stage + (int64_t)s * lim * sd + r * 4, cb + (int64_t)s * slots * sd + r * 4);
+  }
+}
+
 // ---------------------------------------------------------------------------
-// Quantised sub-table geometry.  Entry = G 8-bit codes of one (subspace s,
-// centroid j).  Rows are 128 B (one shared-memory wavefront).  Lane L at step
-// u reads subspace (u + L) mod CS, and each row stores copies / row blocks
-// such that the lanes of one wavefront always hit distinct columns: every
-// lookup is bank-conflict free whatever the code bytes are.
+// Quantised sub-table geometry.  One entry holds the codes of the GT query
+// heads for one (subspace s, centroid j) in 16-bit lanes: GT <= 2 -> 4 bytes,
+// GT = 4 -> 8 bytes {h0|h2, h1|h3}, GT = 8 -> 16 bytes.  Rows are 128 B (one
+// shared-memory wavefront of COLS lanes).  Lane L at step u reads subspace
+// (u + L) mod CS; each row holds copies (or row blocks) placed so that the
+// lanes of one wavefront always hit distinct columns, whatever the codes are.
 // ---------------------------------------------------------------------------
 template <int CS, int GT>
 struct QGeo {
-  static constexpr int EW = (GT <= 4) ? 4 : 8;
+  static constexpr int EW = (GT <= 2) ? 4 : (GT == 4 ? 8 : 16);
   static constexpr int COLS = 128 / EW;
   static constexpr int RB = (CS > COLS) ? CS / COLS : 1;
+  static constexpr int NC = (CS < COLS) ? COLS / CS : 1;
   static constexpr int BYTES = RB * 256 * 128;
   static constexpr int NACC = (GT == 8) ? 4 : (GT == 4 ? 2 : 1);
   static constexpr int W = CS / 4;
-  __device__ static __forceinline__ int col_of(int lane, int s) {
+  __host__ __device__ static constexpr int col_of(int lane, int s) {
     return (CS <= COLS) ? (((lane % COLS) / CS) * CS + s) : (s % COLS);
   }
-  __device__ static __forceinline__ int rb_of(int s) { return (CS <= COLS) ? 0 : s / COLS; }
+  __host__ __device__ static constexpr int rb_of(int s) { return (CS <= COLS) ? 0 : s / COLS; }
 };
 
-template <int W>
-__device__ __forceinline__ void load_code(const uint8_t* p, uint32_t (&w)[W]) {
-  if constexpr (W == 1) {
-    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
-  } else if constexpr (W == 2) {
-    uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-    w[0] = v.x; w[1] = v.y;
-  } else if constexpr (W == 4) {
-    uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
-    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-  } else {
-    uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-    uint4 c = __ldg(reinterpret_cast<const uint4*>(p) + 1);
-    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
-    w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
+__host__ __device__ __forceinline__ int qmax_for(int M) { return 65535 / M; }
+
+template <int GT>
+__device__ __forceinline__ int approx_of(const uint32_t* acc, int g) {
+  // packing: acc[0] = h0 | h2 << 16, acc[1] = h1 | h3 << 16, acc[2] = h4 | h6 << 16, acc[3] = h5 | h7 << 16
+  if constexpr (GT == 1) return (int)acc[0];
+  else if constexpr (GT == 2) return (int)(g == 0 ? (acc[0] & 0xffffu) : (acc[0] >> 16));
+  else {
+    const uint32_t a = acc[(g >> 2) * 2 + (g & 1)];
+    return (int)((g & 2) ? (a >> 16) : (a & 0xffffu));
   }
 }
 
@@ -120,73 +156,129 @@ __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
   for (int i = 0; i < W; ++i) w[i] = t[i];
 }
 
-template <int GT>
-__device__ __forceinline__ int approx_of(const uint32_t* acc, int g) {
-  // packing: acc[0] = h0 | h2 << 16, acc[1] = h1 | h3 << 16, acc[2] = h4 | h6 << 16, acc[3] = h5 | h7 << 16
-  if constexpr (GT == 1) return (int)acc[0];
-  else if constexpr (GT == 2) return (int)(g == 0 ? (acc[0] & 0xffffu) : (acc[0] >> 16));
-  else {
-    const uint32_t a = acc[(g >> 2) * 2 + (g & 1)];
-    return (int)((g & 2) ? (a >> 16) : (a & 0xffffu));
+// ===========================================================================
+// K5: exact and quantised sub-tables, one CTA (512 threads) per (b, KV head).
+// Thread t owns centroid j = t % 256 of the subspaces s = t / 256 + 2i.
+// ===========================================================================
+template <int CS, int GT>
+__global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
+  using Q = QGeo<CS, GT>;
+  constexpr int SPT = (CS + 1) / 2;  // subspaces per thread
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* img = smem;                                   // Q::BYTES
+  float* stage = reinterpret_cast<float*>(smem + Q::BYTES);    // <= 64 KB
+  float* sq = stage + 16384;                                   // [GT][D]
+  __shared__ unsigned s_lo[GT * CS], s_hi[GT * CS];
+  __shared__ float s_lof[GT * CS], s_inv[GT];
+  __shared__ int s_k[32];
+
+  pdl_launch_dependents();
+  const int u = blockIdx.x;
+  const int b = u / p.Hkv, h = u - b * p.Hkv;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const ColdRange cr = cold_range(p, b);
+  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking needed for this sequence
+  const int D = p.D, M = p.M, sd = p.sd;
+  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+  const int lim = stage_rows(p.slots, M * sd);
+  const bool staged = (sd % 4) == 0;
+  if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K5_THREADS);
+  for (int i = tid; i < GT * D; i += K5_THREADS) {
+    const int g = i / D, d = i - g * D;
+    sq[i] = (g < p.G) ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
   }
-}
-
-// ---- async copies and programmatic dependent launch ------------------------
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-// Let the next kernel in the stream start its independent prologue now.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
-// Block until the previous kernel in the stream has completed and its writes are visible.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-
-// Rows [0, lim) of every subspace of one (sequence, KV head) codebook are
-// staged in shared memory as stage[s][j][sd]; lim keeps the stage <= 64 KB.
-__device__ __forceinline__ int stage_rows(int slots, int D) {
-  const int lim = 16384 / D;  // D floats per (row of all subspaces) -> 64 KB
-  return slots < lim ? slots : lim;
-}
-
-__device__ __forceinline__ void stage_codebook(float* stage, const float* cb, int M, int slots, int sd, int lim,
-                                               int tid, int nthreads) {
-  // bytes per subspace block = lim * sd * 4 (multiple of 16 for sd % 4 == 0)
-  const int per_s = lim * sd / 4;  // 16-byte pieces per subspace
-  const int total = M * per_s;
-  for (int i = tid; i < total; i += nthreads) {
-    const int s = i / per_s, r = i - s * per_s;
-    cp_async16(stage + (int64_t)s * lim * sd + r * 4, cb + (int64_t)s * slots * sd + r * 4);
+  if (tid < M) {
+    const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+    s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
   }
-}
+  for (int i = tid; i < GT * CS; i += K5_THREADS) { s_lo[i] = 0xffffffffu; s_hi[i] = 0u; }
+  for (int i = tid; i < Q::BYTES / 16; i += K5_THREADS) reinterpret_cast<uint4*>(img)[i] = make_uint4(0, 0, 0, 0);
+  cp_async_wait_all();
+  __syncthreads();
 
-// Rotate W words so that out[i] = in[(i + r) % W] (r dynamic, W a power of two).
-template <int W, typename T>
-__device__ __forceinline__ void rotate_words(T (&w)[W], int r) {
+  const int j = tid & 255, half = tid >> 8;
+  float tv[GT][SPT];
 #pragma unroll
-  for (int bit = 1; bit < W; bit <<= 1) {
-    T t[W];
-    const bool on = (r & bit) != 0;
+  for (int i = 0; i < SPT; ++i) {
+    const int s = half + 2 * i;
 #pragma unroll
-    for (int i = 0; i < W; ++i) t[i] = on ? w[(i + bit) % W] : w[i];
+    for (int g = 0; g < GT; ++g) tv[g][i] = 0.f;
+    if (s < M) {   // uniform within a warp (a warp never straddles the two halves)
+      if (j < s_k[s]) {
+        const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
+                                               : cbase + ((int64_t)s * p.slots + j) * sd;
 #pragma unroll
-    for (int i = 0; i < W; ++i) w[i] = t[i];
+        for (int g = 0; g < GT; ++g) tv[g][i] = dot_order(p.lut_order, sq + g * D + s * sd, row, sd);
+      }
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        const unsigned o = ord_f32(tv[g][i]);
+        const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
+        if (lane == 0) { atomicMin(&s_lo[g * CS + s], mn); atomicMax(&s_hi[g * CS + s], mx); }
+      }
+    }
   }
+  __syncthreads();
+  const int qmax = qmax_for(M);
+  if (tid < GT) {
+    const int g = tid;
+    float rmax = 0.f;
+    double sa = 0.0;
+    for (int s = 0; s < M; ++s) {
+      const float lo = unord_f32(s_lo[g * CS + s]), hi = unord_f32(s_hi[g * CS + s]);
+      s_lof[g * CS + s] = lo;
+      rmax = fmaxf(rmax, hi - lo);
+      sa += fmax(fabs((double)lo), fabs((double)hi));
+    }
+    // Error budget in code units: entry rounding (<= 0.5 + fp32 slop) for both
+    // tokens of a comparison, the fp32 summation error of the exact scores and
+    // ties created by the final scale multiply.
+    const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
+    const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
+    const bool ok_scale = (p.scale > 0.f) && isfinite(p.scale) && isfinite(sa);
+    s_inv[g] = rmax > 0.f ? (float)qmax / rmax : 0.f;
+    p.margin[(int64_t)u * GT + g] = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
+  }
+  __syncthreads();
+  float* tex = p.texact + (int64_t)u * GT * CS * 256;
+#pragma unroll
+  for (int i = 0; i < SPT; ++i) {
+    const int s = half + 2 * i;
+    if (s >= M) continue;
+    uint32_t c[GT];
+#pragma unroll
+    for (int g = 0; g < GT; ++g) {
+      tex[(g * CS + s) * 256 + j] = tv[g][i];
+      float x = __fmul_rn(__fsub_rn(tv[g][i], s_lof[g * CS + s]), s_inv[g]);
+      x = fminf(fmaxf(rintf(x), 0.f), (float)qmax);
+      c[g] = (uint32_t)x;
+    }
+    for (int copy = 0; copy < Q::NC; ++copy) {
+      const int e = (Q::rb_of(s) * 256 + j) * Q::COLS + copy * CS + (s % Q::COLS);
+      if constexpr (GT == 1) reinterpret_cast<uint32_t*>(img)[e] = c[0];
+      else if constexpr (GT == 2) reinterpret_cast<uint32_t*>(img)[e] = c[0] | (c[1] << 16);
+      else if constexpr (GT == 4) reinterpret_cast<uint2*>(img)[e] = make_uint2(c[0] | (c[2] << 16), c[1] | (c[3] << 16));
+      else
+        reinterpret_cast<uint4*>(img)[e] = make_uint4(c[0] | (c[2] << 16), c[1] | (c[3] << 16),
+                                                      c[4] | (c[6] << 16), c[5] | (c[7] << 16));
+    }
+  }
+  __syncthreads();
+  uint4* gimg = reinterpret_cast<uint4*>(p.qimg + (int64_t)u * p.qimg_bytes);
+  for (int i = tid; i < Q::BYTES / 16; i += K5_THREADS) gimg[i] = reinterpret_cast<const uint4*>(img)[i];
 }
 
+// ===========================================================================
+// K6: candidate stream, grid (chunks, B*H_kv), 256 threads.
+// ===========================================================================
 template <int CS, int GT, int TPTM>
 __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   using Q = QGeo<CS, GT>;
-  static_assert(CS <= Q::COLS, "one row block");
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* qlut = smem;                                            // Q::BYTES
-  float* stage = reinterpret_cast<float*>(smem + Q::BYTES);              // codebook rows, then codes
-  const int stage_bytes = max(64 * 1024, p.chunk * CS);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES + stage_bytes);  // [GT][256]
-  float* sq = reinterpret_cast<float*>(hist + GT * 256);                 // [GT][D]
-  __shared__ unsigned s_lo[GT * CS], s_hi[GT * CS];
-  __shared__ float s_inv[GT], s_lof[GT * CS];
-  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_k[32];
+  unsigned char* qlut = smem;                                              // Q::BYTES
+  unsigned char* scodes = smem + Q::BYTES;                                 // chunk * CS
+  uint32_t* hist = reinterpret_cast<uint32_t*>(scodes + p.chunk * CS);     // [GT][REFINE_BINS]
+  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_alb[GT], s_sh2[GT];
 
   pdl_launch_dependents();
   const int u = blockIdx.y, c = blockIdx.x;
@@ -199,127 +291,35 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     if (tid < GT) cnt_out[tid] = 0;
     return;
   }
-  const int D = p.D, M = p.M, sd = p.sd;
-  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  const int lim = stage_rows(p.slots, D);
-  const bool staged = (sd % 4) == 0;
-
-  // ---- prologue: stage the codebook, load queries and counts ----------------
-  if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K6_THREADS);
-  for (int i = tid; i < GT * D; i += K6_THREADS) {
-    const int g = i / D, d = i - g * D;
-    sq[i] = (g < p.G) ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
-  }
-  if (tid < M) {
-    int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
-    s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-  }
-  for (int i = tid; i < GT * 256; i += K6_THREADS) hist[i] = 0;
-  for (int i = tid; i < GT * CS; i += K6_THREADS) { s_lo[i] = 0xffffffffu; s_hi[i] = 0u; }
-  if (tid < GT) s_cnt[tid] = 0;
-  cp_async_wait_all();
-  __syncthreads();
-
-  // exact sub-table value T[g][s][j] in the reference's BLAS order; j = tid
-  const int j = tid;
-  auto tval = [&](int g, int s) -> float {
-    if (j >= s_k[s]) return 0.f;
-    const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
-                                           : cbase + ((int64_t)s * p.slots + j) * sd;
-    return dot_order(p.lut_order, sq + g * D + s * sd, row, sd);
-  };
-
-  // ---- pass 1: per (head, subspace) value ranges -----------------------------
-  for (int s = 0; s < M; ++s) {
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      const unsigned o = ord_f32(tval(g, s));
-      const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
-      if (lane == 0) { atomicMin(&s_lo[g * CS + s], mn); atomicMax(&s_hi[g * CS + s], mx); }
-    }
-  }
-  __syncthreads();
-  if (tid < GT) {
-    const int g = tid;
-    float rmax = 0.f;
-    double sa = 0.0;
-    for (int s = 0; s < M; ++s) {
-      const float lo = unord_f32(s_lo[g * CS + s]), hi = unord_f32(s_hi[g * CS + s]);
-      s_lof[g * CS + s] = lo;
-      rmax = fmaxf(rmax, hi - lo);
-      sa += fmax(fabs((double)lo), fabs((double)hi));
-    }
-    // Error budget in code units: rounding of each entry (<= 0.5 + fp32 slop)
-    // for both tokens of a comparison, plus the fp32 summation error of the
-    // exact scores and ties created by the final scale multiply.
-    const double delta = rmax > 0.f ? (double)rmax / 255.0 : 1.0;
-    const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
-    const bool ok_scale = (p.scale > 0.f) && isfinite(p.scale) && isfinite(sa);
-    s_inv[g] = rmax > 0.f ? 255.f / rmax : 0.f;
-    s_margin[g] = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
-  }
-  __syncthreads();
-
-  // ---- pass 2: quantise and store the replicated 8-bit sub-tables -----------
-  {
-    using EntT = typename std::conditional<Q::EW == 4, uint32_t, uint2>::type;
-    EntT w[CS];
-#pragma unroll
-    for (int s = 0; s < CS; ++s) {
-      uint32_t code[GT];
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        uint32_t cv = 0;
-        if (s < M) {
-          float x = __fmul_rn(__fsub_rn(tval(g, s), s_lof[g * CS + s]), s_inv[g]);
-          x = fminf(fmaxf(rintf(x), 0.f), 255.f);
-          cv = (uint32_t)x;
-        }
-        code[g] = cv;
-      }
-      if constexpr (GT == 1) w[s] = code[0];
-      else if constexpr (GT == 2) w[s] = code[0] | (code[1] << 16);
-      else if constexpr (GT == 4) w[s] = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
-      else {
-        uint2 v;
-        v.x = code[0] | (code[1] << 8) | (code[2] << 16) | (code[3] << 24);
-        v.y = code[4] | (code[5] << 8) | (code[6] << 16) | (code[7] << 24);
-        w[s] = v;
-      }
-    }
-    // lane L writes subspace (i + L) mod CS at step i: distinct columns per wavefront
-    rotate_words<CS>(w, lane % CS);
-    constexpr int NC = Q::COLS / CS;
-#pragma unroll
-    for (int cp = 0; cp < NC; ++cp) {
-      const int copy = (cp + (lane % Q::COLS) / CS) % NC;
-#pragma unroll
-      for (int i = 0; i < CS; ++i) {
-        const int col = copy * CS + ((i + lane) % CS);
-        reinterpret_cast<EntT*>(qlut)[j * Q::COLS + col] = w[i];
-      }
-    }
-  }
-  __syncthreads();  // codebook stage is dead: reuse it for the chunk's codes
-
-  // ---- stage the chunk's codes -------------------------------------------------
+  const int M = p.M;
+  // ---- prefetch this chunk's codes (independent of the tables) -------------
   const int t0 = c * p.chunk;
   const int ntok = min(p.chunk, cr.Sc - t0);
   const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh + (int64_t)t0 * CS;
   {
     const int n16 = (ntok * CS + 15) / 16;
-    unsigned char* dst = reinterpret_cast<unsigned char*>(stage);
-    for (int i = tid; i < n16; i += K6_THREADS) cp_async16(dst + i * 16, gcodes + (int64_t)i * 16);
-    cp_async_wait_all();
+    for (int i = tid; i < n16; i += K6_THREADS) cp_async16(scodes + i * 16, gcodes + (int64_t)i * 16);
   }
+  for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
+  if (tid < GT) s_cnt[tid] = 0;
+  // ---- tables from K5 --------------------------------------------------------
+  pdl_wait();
+  {
+    const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
+    for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
+  }
+  if (tid < GT) s_margin[tid] = p.margin[(int64_t)u * GT + tid];
+  cp_async_wait_all();
   __syncthreads();
 
-  // ---- 8-bit approximate scores, kept in registers ---------------------------
-  const unsigned char* scodes = reinterpret_cast<const unsigned char*>(stage);
+  // ---- quantised scores, kept in registers -----------------------------------
   const int r = lane % CS;
   int colidx[CS];
 #pragma unroll
-  for (int uu = 0; uu < CS; ++uu) colidx[uu] = Q::col_of(lane, (uu + r) % CS);
+  for (int uu = 0; uu < CS; ++uu) {
+    const int s = (uu + r) % CS;
+    colidx[uu] = Q::rb_of(s) * 256 * Q::COLS + Q::col_of(lane, s);
+  }
   uint32_t accs[TPTM][Q::NACC];
   int mxv[GT];
 #pragma unroll
@@ -332,7 +332,6 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     if (it >= tpt) continue;
     const int lt = it * K6_THREADS + tid;
     const int t = t0 + lt;
-    const bool valid = t >= lo_t && t < hi_t;
     uint32_t w[Q::W];
     if constexpr (Q::W == 1) w[0] = *reinterpret_cast<const uint32_t*>(scodes + lt * CS);
     else if constexpr (Q::W == 2) { const uint2 v = *reinterpret_cast<const uint2*>(scodes + lt * CS); w[0] = v.x; w[1] = v.y; }
@@ -349,49 +348,46 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
       const uint32_t byte = (w[uu >> 2] >> (8 * (uu & 3))) & 0xffu;
       const int e = colidx[uu] + (int)byte * Q::COLS;
       if constexpr (Q::EW == 4) {
-        const uint32_t x = reinterpret_cast<const uint32_t*>(qlut)[e];
-        if constexpr (GT <= 2) {
-          accs[it][0] += x;
-        } else {
-          accs[it][0] += x & 0x00ff00ffu;
-          accs[it][1] += (x >> 8) & 0x00ff00ffu;
-        }
-      } else {
+        accs[it][0] += reinterpret_cast<const uint32_t*>(qlut)[e];
+      } else if constexpr (Q::EW == 8) {
         const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
-        accs[it][0] += x.x & 0x00ff00ffu;
-        accs[it][1] += (x.x >> 8) & 0x00ff00ffu;
-        accs[it][2] += x.y & 0x00ff00ffu;
-        accs[it][3] += (x.y >> 8) & 0x00ff00ffu;
+        accs[it][0] += x.x; accs[it][1] += x.y;
+      } else {
+        const uint4 x = reinterpret_cast<const uint4*>(qlut)[e];
+        accs[it][0] += x.x; accs[it][1] += x.y; accs[it][2] += x.z; accs[it][3] += x.w;
       }
     }
-    if (valid) {
+    if (t >= lo_t && t < hi_t) {
 #pragma unroll
       for (int g = 0; g < GT; ++g) mxv[g] = max(mxv[g], approx_of<GT>(accs[it], g));
     }
   }
 
-  // ---- lower bound of the k'-th largest approximate score ------------------
+  // ---- threshold: coarse (per-thread maxima), then refined (all tokens) -----
+  const int maxv = M * qmax_for(M);
   int sh = 0;
-  while (((M * 255) >> sh) > 255) ++sh;
+  while ((maxv >> sh) > 255) ++sh;
 #pragma unroll
   for (int g = 0; g < GT; ++g)
-    if (mxv[g] >= 0) atomicAdd(&hist[g * 256 + (mxv[g] >> sh)], 1u);
+    if (mxv[g] >= 0) atomicAdd(&hist[g * REFINE_BINS + (mxv[g] >> sh)], 1u);
   __syncthreads();
+  const uint32_t kp = (uint32_t)cr.kp;
   if (warp < GT) {
     const int g = warp;
-    const uint32_t* hg = hist + g * 256;
+    const uint32_t* hg = hist + g * REFINE_BINS;
     uint32_t ls = 0;
+    int top = -1;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ls += hg[lane * 8 + i];
+    for (int i = 0; i < 8; ++i) { const uint32_t v = hg[lane * 8 + i]; ls += v; if (v) top = lane * 8 + i; }
+    top = __reduce_max_sync(0xffffffffu, top + 1) - 1;
     uint32_t suf = ls;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
       if (lane + o < 32) suf += t;
     }
-    const uint32_t kp = (uint32_t)cr.kp;
     const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
-    int thr = -(1 << 30);
+    int alb = -1, sh2 = 0;
     if (ball != 0u) {
       const int lstar = 31 - __clz((int)ball);
       const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
@@ -404,7 +400,55 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
         }
       }
       bstar = __shfl_sync(0xffffffffu, bstar, lstar);
-      thr = (bstar << sh) - s_margin[g];
+      alb = bstar << sh;
+      const int span = ((top + 1) << sh) - alb;
+      while ((span >> sh2) >= REFINE_BINS) ++sh2;
+    }
+    if (lane == 0) { s_alb[g] = alb; s_sh2[g] = sh2; }
+  }
+  __syncthreads();
+  for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < TPTM; ++it) {
+    if (it >= tpt) break;
+    const int t = t0 + it * K6_THREADS + tid;
+    if (t < lo_t || t >= hi_t) continue;
+#pragma unroll
+    for (int g = 0; g < GT; ++g) {
+      const int a = approx_of<GT>(accs[it], g), alb = s_alb[g];
+      if (alb >= 0 && a >= alb) atomicAdd(&hist[g * REFINE_BINS + ((a - alb) >> s_sh2[g])], 1u);
+    }
+  }
+  __syncthreads();
+  if (warp < GT) {
+    const int g = warp;
+    const uint32_t* hg = hist + g * REFINE_BINS;
+    constexpr int PER = REFINE_BINS / 32;
+    uint32_t ls = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ls += hg[lane * PER + i];
+    uint32_t suf = ls;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+      if (lane + o < 32) suf += t;
+    }
+    const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
+    int thr = -(1 << 30);
+    if (s_alb[g] >= 0 && ball != 0u) {
+      const int lstar = 31 - __clz((int)ball);
+      const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
+      int bstar = -1;
+      if (lane == lstar) {
+        uint32_t cum = above;
+        for (int i = PER - 1; i >= 0; --i) {
+          cum += hg[lane * PER + i];
+          if (cum >= kp) { bstar = lane * PER + i; break; }
+        }
+      }
+      bstar = __shfl_sync(0xffffffffu, bstar, lstar);
+      thr = s_alb[g] + (bstar << s_sh2[g]) - s_margin[g];
     }
     if (lane == 0) s_thr[g] = (s_margin[g] >= (1 << 30)) ? -(1 << 30) : thr;
   }
@@ -566,21 +610,101 @@ __device__ __forceinline__ void load_row(const KVT* p, float (&o)[DPL]) {
   }
 }
 
+// ===========================================================================
+// K7: exact selection and attention, grid (B*H_kv*G), 256 threads.
+// ===========================================================================
+template <int D, typename KVT>
+struct Attn {
+  using A = AttnGeo<D>;
+  static constexpr int NW = K7_THREADS / 32;
+  static constexpr int U = 8;
+  float qv[A::DPL];
+  float m_run, l_run, acc[A::DPL];
+  int sub, sl;
+
+  __device__ void init(const float* s_q, int lane) {
+    sub = lane / A::LPT;
+    sl = lane - sub * A::LPT;
+#pragma unroll
+    for (int i = 0; i < A::DPL; ++i) { qv[i] = s_q[sl * A::DPL + i]; acc[i] = 0.f; }
+    m_run = -INFINITY;
+    l_run = 0.f;
+  }
+
+  // Online softmax over tokens i in [0, n) with token index tok(i); the U
+  // scores of a step are reduced together, then folded in with one rescale.
+  template <typename TokF, typename ScoreF>
+  __device__ void run(const KVT* kb, const KVT* vb, int n, int warp, float scale, TokF tok, ScoreF on_score) {
+    constexpr int STEP = NW * A::SUB * U;
+    for (int ib = warp * A::SUB * U; ib < n; ib += STEP) {
+      float kf[U][A::DPL], vf[U][A::DPL], s[U];
+      bool valid[U];
+#pragma unroll
+      for (int r = 0; r < U; ++r) {
+        const int i = ib + r * A::SUB + sub;
+        valid[r] = i < n;
+        if (valid[r]) {
+          const int t = tok(i);
+          load_row<KVT, A::DPL>(kb + (int64_t)t * D + sl * A::DPL, kf[r]);
+          load_row<KVT, A::DPL>(vb + (int64_t)t * D + sl * A::DPL, vf[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < U; ++r) {
+        s[r] = 0.f;
+        if (valid[r]) {
+#pragma unroll
+          for (int i = 0; i < A::DPL; ++i) s[r] = fmaf(qv[i], kf[r][i], s[r]);
+        }
+      }
+#pragma unroll
+      for (int o = A::LPT / 2; o; o >>= 1) {
+#pragma unroll
+        for (int r = 0; r < U; ++r) s[r] += __shfl_xor_sync(0xffffffffu, s[r], o);
+      }
+      float mloc = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < U; ++r) {
+        if (valid[r]) {
+          s[r] *= scale;
+          on_score(ib + r * A::SUB + sub, s[r]);
+          mloc = fmaxf(mloc, s[r]);
+        }
+      }
+      if (mloc != -INFINITY) {
+        const float mn = fmaxf(m_run, mloc);
+        const float corr = __expf(m_run - mn);
+        l_run *= corr;
+#pragma unroll
+        for (int d = 0; d < A::DPL; ++d) acc[d] *= corr;
+#pragma unroll
+        for (int r = 0; r < U; ++r) {
+          if (valid[r]) {
+            const float pe = __expf(s[r] - mn);
+            l_run += pe;
+#pragma unroll
+            for (int d = 0; d < A::DPL; ++d) acc[d] = fmaf(pe, vf[r][d], acc[d]);
+          }
+        }
+        m_run = mn;
+      }
+    }
+  }
+};
+
 template <int D, typename KVT>
 __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   using A = AttnGeo<D>;
-  constexpr int NW = K7_THREADS / 32;
-  constexpr int U = 8;
+  using AT = Attn<D, KVT>;
+  constexpr int NW = AT::NW;
   extern __shared__ __align__(16) unsigned char smem[];
   float* T = reinterpret_cast<float*>(smem);                                 // [M][256] exact sub-table
-  unsigned char* X = smem + p.M * 1024;                                      // prologue: codebook stage;
-  float* stage = reinterpret_cast<float*>(X);                                // afterwards the buffers below
-  uint64_t* keys = reinterpret_cast<uint64_t*>(X);                           // [K7_CAP]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(X + K7_CAP * 8);              // [1024]
-  int* sel = reinterpret_cast<int*>(X + K7_CAP * 8 + 4096);                  // [TOPK_MAX]
-  float* part = reinterpret_cast<float*>(X + K7_CAP * 8 + 4096 + TOPK_MAX * 4);  // [NW][D + 2]
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.M * 1024);           // [K7_CAP]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(keys + K7_CAP);               // [1024]
+  int* sel = reinterpret_cast<int*>(hist + 1024);                            // [TOPK_MAX]
+  float* part = reinterpret_cast<float*>(sel + TOPK_MAX);                    // [NW][D + 2]
   __shared__ float s_q[D];
-  __shared__ int s_n, s_k[32], s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
+  __shared__ int s_n, s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
   __shared__ SelShared s_sel;
 
   const int Hq = p.Hkv * p.G;
@@ -590,39 +714,26 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ColdRange cr = cold_range(p, b);
   const bool topk_mode = !(cr.k >= cr.Sc) && cr.kp > 0;
+  const KVT* kb = reinterpret_cast<const KVT*>(p.k) + (int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh;
+  const KVT* vb = reinterpret_cast<const KVT*>(p.v) + (int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh;
+  const float scale = p.scale;
+  const bool want_scores = p.sel_score != nullptr;
+  const int sel_cap = max(p.top_k, p.sink);   // sinks are kept even when top_k < sink_tokens
+  const int64_t sel_base = ((int64_t)b * Hq + hq) * sel_cap;
 
-  // ---- prologue (independent of the candidate stage): q, exact sub-table ----
   for (int d = tid; d < D; d += K7_THREADS)
     s_q[d] = load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)hq * D + d);
   if (tid == 0) s_n = 0;
-  const int M = p.M, sd = p.sd;
-  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  const int lim = stage_rows(p.slots, p.M * sd);
-  const bool staged = (sd % 4) == 0;
-  if (topk_mode) {
-    if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K7_THREADS);
-    if (tid < M) {
-      int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
-      s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-    }
-    cp_async_wait_all();
-  }
   __syncthreads();
-  if (topk_mode) {
-    for (int i = tid; i < M * 256; i += K7_THREADS) {
-      const int s = i >> 8, j = i & 255;
-      float t = 0.f;
-      if (j < s_k[s]) {
-        const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
-                                               : cbase + ((int64_t)s * p.slots + j) * sd;
-        t = dot_order(p.lut_order, s_q + s * sd, row, sd);
-      }
-      T[i] = t;
-    }
-  }
+  AT at;
+  at.init(s_q, lane);
+
+  // ---- hot window: independent of the candidate stage, done before waiting --
+  const int n_hot = cr.S - cr.Sc;
+  at.run(kb, vb, n_hot, warp, scale, [&](int i) { return cr.Sc + i; }, [](int, float) {});
+
   // ---- wait for the candidate stage ------------------------------------------
   pdl_wait();
-  __syncthreads();
 
   int n_sel;
   bool explicit_sel = false;
@@ -632,10 +743,13 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     n_sel = cr.sink;
   } else {
     explicit_sel = true;
-    const float scale = p.scale;
+    const int M = p.M;
+    // exact sub-table of this head (written by K5)
+    const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
+    for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
     const int64_t cbase_idx = (int64_t)u * p.n_chunks * p.GT;
-    // candidate counts of every chunk (-1: list overflowed, rescan the chunk)
     for (int c = tid; c < p.n_chunks; c += K7_THREADS) s_cnt[c] = p.cand_cnt[cbase_idx + (int64_t)c * p.GT + g];
+    cp_async_wait_all();
     __syncthreads();
     if (tid == 0) {
       int acc = 0;
@@ -699,79 +813,33 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     __syncthreads();
   }
 
-  // ---- exact attention over selected cold tokens + hot window ---------------
-  const int n_hot = cr.S - cr.Sc;
-  const int n_tot = n_sel + n_hot;
-  const KVT* kb = reinterpret_cast<const KVT*>(p.k) + (int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh;
-  const KVT* vb = reinterpret_cast<const KVT*>(p.v) + (int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh;
-  const int sub = lane / A::LPT, sl = lane - sub * A::LPT;
-  float qv[A::DPL];
-#pragma unroll
-  for (int i = 0; i < A::DPL; ++i) qv[i] = s_q[sl * A::DPL + i];
-  float m_run = -INFINITY, l_run = 0.f, acc[A::DPL];
-#pragma unroll
-  for (int i = 0; i < A::DPL; ++i) acc[i] = 0.f;
-  const bool want_scores = p.sel_score != nullptr;
-  const int sel_cap = max(p.top_k, p.sink);   // sinks are kept even when top_k < sink_tokens
-  const int64_t sel_base = ((int64_t)b * Hq + hq) * sel_cap;
-  constexpr int STEP = NW * A::SUB * U;
-  for (int ib = warp * A::SUB * U; ib < n_tot; ib += STEP) {
-    float kf[U][A::DPL], vf[U][A::DPL];
-    bool valid[U];
-#pragma unroll
-    for (int r = 0; r < U; ++r) {
-      const int i = ib + r * A::SUB + sub;
-      valid[r] = i < n_tot;
-      if (valid[r]) {
-        const int t = (i < n_sel) ? (explicit_sel ? sel[i] : i) : (cr.Sc + (i - n_sel));
-        load_row<KVT, A::DPL>(kb + (int64_t)t * D + sl * A::DPL, kf[r]);
-        load_row<KVT, A::DPL>(vb + (int64_t)t * D + sl * A::DPL, vf[r]);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < U; ++r) {
-      float s = 0.f;
-      if (valid[r]) {
-#pragma unroll
-        for (int i = 0; i < A::DPL; ++i) s = fmaf(qv[i], kf[r][i], s);
-      }
-#pragma unroll
-      for (int o = A::LPT / 2; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (valid[r]) {
-        s *= p.scale;
-        const int i = ib + r * A::SUB + sub;
-        if (want_scores && sl == 0 && i < n_sel && i < sel_cap) p.sel_score[sel_base + i] = s;
-        const float mn = fmaxf(m_run, s);
-        const float corr = __expf(m_run - mn);
-        const float pe = __expf(s - mn);
-        l_run = l_run * corr + pe;
-#pragma unroll
-        for (int d = 0; d < A::DPL; ++d) acc[d] = acc[d] * corr + pe * vf[r][d];
-        m_run = mn;
-      }
-    }
-  }
-  // combine the SUB token groups of this warp
+  // ---- exact attention over the selected cold tokens ------------------------
+  at.run(kb, vb, n_sel, warp, scale, [&](int i) { return explicit_sel ? sel[i] : i; },
+         [&](int i, float s) {
+           if (want_scores && at.sl == 0 && i < sel_cap) p.sel_score[sel_base + i] = s;
+         });
+
+  // combine the SUB token groups of this warp, then the warps
 #pragma unroll
   for (int o = A::LPT; o < 32; o <<= 1) {
-    const float mo = __shfl_xor_sync(0xffffffffu, m_run, o);
-    const float lo = __shfl_xor_sync(0xffffffffu, l_run, o);
-    const float mn = fmaxf(m_run, mo);
-    const float a = (m_run == -INFINITY) ? 0.f : __expf(m_run - mn);
+    const float mo = __shfl_xor_sync(0xffffffffu, at.m_run, o);
+    const float lo = __shfl_xor_sync(0xffffffffu, at.l_run, o);
+    const float mn = fmaxf(at.m_run, mo);
+    const float a = (at.m_run == -INFINITY) ? 0.f : __expf(at.m_run - mn);
     const float c = (mo == -INFINITY) ? 0.f : __expf(mo - mn);
-    l_run = l_run * a + lo * c;
+    at.l_run = at.l_run * a + lo * c;
 #pragma unroll
     for (int d = 0; d < A::DPL; ++d) {
-      const float ao = __shfl_xor_sync(0xffffffffu, acc[d], o);
-      acc[d] = acc[d] * a + ao * c;
+      const float ao = __shfl_xor_sync(0xffffffffu, at.acc[d], o);
+      at.acc[d] = at.acc[d] * a + ao * c;
     }
-    m_run = mn;
+    at.m_run = mn;
   }
   float* pw = part + warp * (D + 2);
-  if (sub == 0) {
+  if (at.sub == 0) {
 #pragma unroll
-    for (int d = 0; d < A::DPL; ++d) pw[sl * A::DPL + d] = acc[d];
-    if (sl == 0) { pw[D] = m_run; pw[D + 1] = l_run; }
+    for (int d = 0; d < A::DPL; ++d) pw[at.sl * A::DPL + d] = at.acc[d];
+    if (at.sl == 0) { pw[D] = at.m_run; pw[D + 1] = at.l_run; }
   }
   __syncthreads();
   for (int d = tid; d < D; d += K7_THREADS) {

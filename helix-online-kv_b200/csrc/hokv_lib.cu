@@ -59,43 +59,11 @@ static int ensure_smem(K kernel, size_t bytes) {
   return HOKV_OK;
 }
 
-template <int CS, int GT>
-static int launch_k6(const Cdc03P& p, cudaStream_t st) {
-  using Q = QGeo<CS, GT>;
-  constexpr int TPTM = GT == 8 ? 8 : 16;
-  if (p.chunk > TPTM * K6_THREADS || (size_t)p.chunk * CS > 64 * 1024)
-    return fail(HOKV_ERR_INVALID, "cdc03: chunk %d too large for this variant", p.chunk);
-  const size_t stage = std::max<size_t>(64 * 1024, (size_t)p.chunk * CS);
-  const size_t sm = Q::BYTES + stage + (size_t)GT * 1024 + (size_t)GT * p.D * 4;
-  if (int e = ensure_smem(k6_candidates<CS, GT, TPTM>, sm)) return e;
-  dim3 grid((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
-  k6_candidates<CS, GT, TPTM><<<grid, K6_THREADS, sm, st>>>(p);
-  return check_launch("k6_candidates");
-}
-
-static int dispatch_k6(const Cdc03P& p, cudaStream_t st) {
-#define HOKV_K6(cs_, gt_) if (p.CS == cs_ && p.GT == gt_) return launch_k6<cs_, gt_>(p, st);
-  HOKV_K6(4, 1) HOKV_K6(4, 2) HOKV_K6(4, 4) HOKV_K6(4, 8)
-  HOKV_K6(8, 1) HOKV_K6(8, 2) HOKV_K6(8, 4) HOKV_K6(8, 8)
-  HOKV_K6(16, 1) HOKV_K6(16, 2) HOKV_K6(16, 4) HOKV_K6(16, 8)
-  HOKV_K6(32, 1) HOKV_K6(32, 2) HOKV_K6(32, 4)
-#undef HOKV_K6
-  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: no K6 variant for code_bytes=%d group=%d", p.CS, p.GT);
-}
-
-// K7 is launched with programmatic stream serialization: its prologue (query,
-// codebook stage, exact sub-table) overlaps the tail of K6, and it blocks in
-// griddepcontrol.wait before reading K6's candidate lists.
-template <int D, typename KVT>
-static int launch_k7(const Cdc03P& p, cudaStream_t st) {
-  const int lim = std::min(p.slots, 16384 / (p.M * p.sd));
-  const size_t stage = (size_t)p.M * lim * p.sd * 4;
-  const size_t bufs = (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 + (size_t)(K7_THREADS / 32) * (D + 2) * 4;
-  const size_t sm = (size_t)p.M * 1024 + std::max(stage, bufs);
-  if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
+template <typename K>
+static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st, const Cdc03P& p, const char* what) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.B * p.Hkv * p.G));
-  cfg.blockDim = dim3(K7_THREADS);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.dynamicSmemBytes = sm;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -103,9 +71,54 @@ static int launch_k7(const Cdc03P& p, cudaStream_t st) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k7_select_attend<D, KVT>, p);
-  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "k7_select_attend launch: %s", cudaGetErrorString(e));
-  return check_launch("k7_select_attend");
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
+// Stage 1: K5 (tables, ordinary launch: it reads the queries) then K6
+// (candidates, programmatic launch: it prefetches its codes while K5 runs).
+template <int CS, int GT>
+static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
+  using Q = QGeo<CS, GT>;
+  constexpr int TPTM = GT == 8 ? 8 : 16;
+  if (p.chunk > TPTM * K6_THREADS || (size_t)p.chunk * CS > 64 * 1024)
+    return fail(HOKV_ERR_INVALID, "cdc03: chunk %d too large for this variant", p.chunk);
+  const size_t sm5 = Q::BYTES + 65536 + (size_t)GT * p.D * 4;
+  if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
+  k5_tables<CS, GT><<<(unsigned)(p.B * p.Hkv), K5_THREADS, sm5, st>>>(p);
+  if (int e = check_launch("k5_tables")) return e;
+  const size_t sm6 = Q::BYTES + (size_t)p.chunk * CS + (size_t)GT * REFINE_BINS * 4;
+  if (int e = ensure_smem(k6_candidates<CS, GT, TPTM>, sm6)) return e;
+  return launch_pdl(k6_candidates<CS, GT, TPTM>, dim3((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv)),
+                    dim3(K6_THREADS), sm6, st, p, "k6_candidates");
+}
+
+static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
+#define HOKV_S1(cs_, gt_) if (p.CS == cs_ && p.GT == gt_) return launch_stage1<cs_, gt_>(p, st);
+  HOKV_S1(4, 1) HOKV_S1(4, 2) HOKV_S1(4, 4) HOKV_S1(4, 8)
+  HOKV_S1(8, 1) HOKV_S1(8, 2) HOKV_S1(8, 4) HOKV_S1(8, 8)
+  HOKV_S1(16, 1) HOKV_S1(16, 2) HOKV_S1(16, 4) HOKV_S1(16, 8)
+  HOKV_S1(32, 1) HOKV_S1(32, 2) HOKV_S1(32, 4)
+#undef HOKV_S1
+  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: no candidate-stage variant for code_bytes=%d group=%d", p.CS, p.GT);
+}
+
+static int qimg_bytes_for(int CS, int GT) {
+  const int ew = GT <= 2 ? 4 : (GT == 4 ? 8 : 16);
+  const int cols = 128 / ew;
+  const int rb = CS > cols ? CS / cols : 1;
+  return rb * 256 * 128;
+}
+
+// Stage 2: K7, programmatic launch (hot-window attention overlaps K6).
+template <int D, typename KVT>
+static int launch_k7(const Cdc03P& p, cudaStream_t st) {
+  const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 +
+                    (size_t)(K7_THREADS / 32) * (D + 2) * 4;
+  if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
+  return launch_pdl(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
+                    "k7_select_attend");
 }
 
 template <typename KVT>
@@ -123,7 +136,7 @@ static int dispatch_k7(const Cdc03P& p, int kv_dtype, cudaStream_t st) {
   if (kv_dtype == HOKV_BF16) return dispatch_k7_t<__nv_bfloat16>(p, st);
   if (kv_dtype == HOKV_F16) return dispatch_k7_t<__half>(p, st);
   if (kv_dtype == HOKV_F32) return dispatch_k7_t<float>(p, st);
-  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: head_dim %d", p.D);
+  return fail(HOKV_ERR_UNSUPPORTED, "cdc03: kv dtype %d", kv_dtype);
 }
 
 }  // namespace hokv
@@ -390,8 +403,11 @@ int hokv_pq_value_output(const double* weights, int64_t seq_len, const uint8_t* 
 static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct Plan {
-  int n_chunks, chunk, GT;
-  size_t cand_idx_bytes, cand_cnt_bytes, cand_code_bytes;
+  int n_chunks, chunk, GT, qimg_bytes;
+  size_t cand_idx_bytes, cand_cnt_bytes, cand_code_bytes, qimg_total, texact_bytes, margin_bytes;
+  size_t total() const {
+    return cand_idx_bytes + cand_cnt_bytes + cand_code_bytes + qimg_total + texact_bytes + margin_bytes;
+  }
 };
 
 static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
@@ -442,13 +458,17 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
   pl->cand_idx_bytes = a256(slots * 4);
   pl->cand_cnt_bytes = a256((size_t)units * pl->n_chunks * pl->GT * 4);
   pl->cand_code_bytes = a256(slots * a->code_bytes);
+  pl->qimg_bytes = qimg_bytes_for(a->code_bytes, pl->GT);
+  pl->qimg_total = a256((size_t)units * pl->qimg_bytes);
+  pl->texact_bytes = a256((size_t)units * pl->GT * a->code_bytes * 256 * 4);
+  pl->margin_bytes = a256((size_t)units * pl->GT * 4);
   return HOKV_OK;
 }
 
 int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes) {
   Plan pl;
   if (int st = plan_cdc03(a, &pl)) return st;
-  *bytes = pl.cand_idx_bytes + pl.cand_cnt_bytes + pl.cand_code_bytes;
+  *bytes = pl.total();
   return HOKV_OK;
 }
 
@@ -468,7 +488,15 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   unsigned char* w = static_cast<unsigned char*>(a->workspace);
   p.cand_idx = reinterpret_cast<uint32_t*>(w);
   p.cand_cnt = reinterpret_cast<int*>(w + pl.cand_idx_bytes);
-  p.cand_code = w + pl.cand_idx_bytes + pl.cand_cnt_bytes;
+  w += pl.cand_idx_bytes + pl.cand_cnt_bytes;
+  p.cand_code = w;
+  w += pl.cand_code_bytes;
+  p.qimg = w;
+  w += pl.qimg_total;
+  p.texact = reinterpret_cast<float*>(w);
+  w += pl.texact_bytes;
+  p.margin = reinterpret_cast<int*>(w);
+  p.qimg_bytes = pl.qimg_bytes;
   p.n_chunks = pl.n_chunks; p.chunk = pl.chunk; p.GT = pl.GT;
   return p;
 }
@@ -476,7 +504,7 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
 static int cdc03_prepare(const hokv_cdc03_args* a, Cdc03P* p) {
   Plan pl;
   if (int st = plan_cdc03(a, &pl)) return st;
-  const size_t need = pl.cand_idx_bytes + pl.cand_cnt_bytes + pl.cand_code_bytes;
+  const size_t need = pl.total();
   if (!a->workspace || a->workspace_bytes < need)
     return fail(HOKV_ERR_WORKSPACE, "cdc03: workspace %zu < %zu", a->workspace_bytes, need);
   HOKV_REQUIRE(aligned(a->workspace, 16), "cdc03: workspace must be 16-byte aligned");
@@ -487,7 +515,7 @@ static int cdc03_prepare(const hokv_cdc03_args* a, Cdc03P* p) {
 int hokv_cdc03_candidates(const hokv_cdc03_args* a, void* stream) {
   Cdc03P p;
   if (int st = cdc03_prepare(a, &p)) return st;
-  return dispatch_k6(p, S(stream));
+  return dispatch_stage1(p, S(stream));
 }
 
 int hokv_cdc03_attend(const hokv_cdc03_args* a, void* stream) {
@@ -499,7 +527,7 @@ int hokv_cdc03_attend(const hokv_cdc03_args* a, void* stream) {
 int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream) {
   Cdc03P p;
   if (int st = cdc03_prepare(a, &p)) return st;
-  if (int st = dispatch_k6(p, S(stream))) return st;
+  if (int st = dispatch_stage1(p, S(stream))) return st;
   return dispatch_k7(p, a->kv_dtype, S(stream));
 }
 
