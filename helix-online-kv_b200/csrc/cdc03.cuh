@@ -21,11 +21,12 @@
 // product_codebook.py:172-227 (tables, gather).
 #pragma once
 #include "hokv_common.cuh"
+#include <cooperative_groups.h>
 #include <type_traits>
 
 namespace hokv {
 
-constexpr int K5_THREADS = 512;
+constexpr int K5_THREADS = 256;
 constexpr int K6_THREADS = 256;
 constexpr int K6_CHUNK_MAX = 4096;   // tokens per K6 CTA (16 per thread)
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
@@ -136,6 +137,24 @@ __device__ __forceinline__ int approx_of(const uint32_t* acc, int g) {
   }
 }
 
+template <int W>
+__device__ __forceinline__ void load_code(const uint8_t* p, uint32_t (&w)[W]) {
+  if constexpr (W == 1) {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  } else if constexpr (W == 2) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  } else if constexpr (W == 4) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint4 c = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = c.x; w[5] = c.y; w[6] = c.z; w[7] = c.w;
+  }
+}
+
 // Rotate a W-word byte string left by r bytes: out byte u = in byte (u + r) mod 4W.
 template <int W>
 __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
@@ -157,76 +176,88 @@ __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
 }
 
 // ===========================================================================
-// K5: exact and quantised sub-tables, one CTA (512 threads) per (b, KV head).
-// Thread t owns centroid j = t % 256 of the subspaces s = t / 256 + 2i.
+// K5: exact and quantised sub-tables, one CTA (256 threads) per (b, KV head,
+// query head g).  The centroid rows are staged in shared memory; thread t
+// owns centroid j = t % kpad of the subspaces s = t / kpad + i * (256 / kpad),
+// kpad = the centroid count rounded up to a power of two >= 32, so the CTA
+// runs max(1, 256 / kpad) subspaces at a time.  Each CTA writes its head's
+// 16-bit lane of the packed entries, its exact fp32 table and its margin.
 // ===========================================================================
-template <int CS, int GT>
-__global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
-  using Q = QGeo<CS, GT>;
-  constexpr int SPT = (CS + 1) / 2;  // subspaces per thread
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* img = smem;                                   // Q::BYTES
-  float* stage = reinterpret_cast<float*>(smem + Q::BYTES);    // <= 64 KB
-  float* sq = stage + 16384;                                   // [GT][D]
-  __shared__ unsigned s_lo[GT * CS], s_hi[GT * CS];
-  __shared__ float s_lof[GT * CS], s_inv[GT];
-  __shared__ int s_k[32];
+template <int SD>
+__device__ __forceinline__ float lut_dot(const float* q, const float* c) {
+  // GEMV order of NumPy/OpenBLAS for (1 x SD) @ (SD x k); see hokv_math.cuh
+  return dot_gemv(q, c, SD);
+}
 
-  pdl_launch_dependents();
-  const int u = blockIdx.x;
+template <int CS, int GT, int SD>
+__device__ __forceinline__ void k5_body(const Cdc03P& p, unsigned char* smem) {
+  using Q = QGeo<CS, GT>;
+  float* stage = reinterpret_cast<float*>(smem);               // <= 64 KB
+  __shared__ float sq[256];
+  __shared__ unsigned s_lo[CS], s_hi[CS];
+  __shared__ float s_lof[CS], s_inv;
+  __shared__ int s_k[32], s_kmax;
+
+  const int u = blockIdx.x, g = blockIdx.y;
   const int b = u / p.Hkv, h = u - b * p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31;
   const ColdRange cr = cold_range(p, b);
   if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking needed for this sequence
-  const int D = p.D, M = p.M, sd = p.sd;
+  const int D = p.D, M = p.M;
   const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  const int lim = stage_rows(p.slots, M * sd);
-  const bool staged = (sd % 4) == 0;
-  if (staged) stage_codebook(stage, cbase, M, p.slots, sd, lim, tid, K5_THREADS);
-  for (int i = tid; i < GT * D; i += K5_THREADS) {
-    const int g = i / D, d = i - g * D;
-    sq[i] = (g < p.G) ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
-  }
+  const int lim = stage_rows(p.slots, M * SD);
+  stage_codebook(stage, cbase, M, p.slots, SD, lim, tid, blockDim.x);
+  const bool real = g < p.G;
+  for (int d = tid; d < D; d += blockDim.x)
+    sq[d] = real ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
   if (tid < M) {
     const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
     s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
   }
-  for (int i = tid; i < GT * CS; i += K5_THREADS) { s_lo[i] = 0xffffffffu; s_hi[i] = 0u; }
-  for (int i = tid; i < Q::BYTES / 16; i += K5_THREADS) reinterpret_cast<uint4*>(img)[i] = make_uint4(0, 0, 0, 0);
+  if (tid < CS) { s_lo[tid] = 0xffffffffu; s_hi[tid] = 0u; }
   cp_async_wait_all();
   __syncthreads();
-
-  const int j = tid & 255, half = tid >> 8;
-  float tv[GT][SPT];
+  if (tid == 0) {
+    int km = 1;
+    for (int s = 0; s < M; ++s) km = max(km, s_k[s]);
+    s_kmax = km;
+  }
+  __syncthreads();
+  int kpad = 32;
+  while (kpad < s_kmax) kpad <<= 1;
+  const int groups = 256 / kpad;            // subspaces processed together
+  const int j = tid % kpad, grp = tid / kpad;
+  constexpr int SPT = CS;                    // upper bound of subspaces per thread
+  float tv[SPT];
+  float qs[SD];
 #pragma unroll
   for (int i = 0; i < SPT; ++i) {
-    const int s = half + 2 * i;
+    const int s = grp + i * groups;
+    tv[i] = 0.f;
+    if (s < M) {   // uniform within a warp: kpad >= 32
 #pragma unroll
-    for (int g = 0; g < GT; ++g) tv[g][i] = 0.f;
-    if (s < M) {   // uniform within a warp (a warp never straddles the two halves)
+      for (int d = 0; d < SD; ++d) qs[d] = sq[s * SD + d];
       if (j < s_k[s]) {
-        const float* row = (staged && j < lim) ? stage + ((int64_t)s * lim + j) * sd
-                                               : cbase + ((int64_t)s * p.slots + j) * sd;
+        const float* row = (j < lim) ? stage + ((int64_t)s * lim + j) * SD : cbase + ((int64_t)s * p.slots + j) * SD;
+        float c[SD];
 #pragma unroll
-        for (int g = 0; g < GT; ++g) tv[g][i] = dot_order(p.lut_order, sq + g * D + s * sd, row, sd);
+        for (int d = 0; d < SD; ++d) c[d] = row[d];
+        tv[i] = lut_dot<SD>(qs, c);
       }
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        const unsigned o = ord_f32(tv[g][i]);
-        const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
-        if (lane == 0) { atomicMin(&s_lo[g * CS + s], mn); atomicMax(&s_hi[g * CS + s], mx); }
-      }
+      const unsigned o = ord_f32(tv[i]);
+      const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
+      if (lane == 0) { atomicMin(&s_lo[s], mn); atomicMax(&s_hi[s], mx); }
     }
   }
   __syncthreads();
   const int qmax = qmax_for(M);
-  if (tid < GT) {
-    const int g = tid;
+  if (tid == 0) {
     float rmax = 0.f;
     double sa = 0.0;
     for (int s = 0; s < M; ++s) {
-      const float lo = unord_f32(s_lo[g * CS + s]), hi = unord_f32(s_hi[g * CS + s]);
-      s_lof[g * CS + s] = lo;
+      float lo = unord_f32(s_lo[s]), hi = unord_f32(s_hi[s]);
+      if (s_k[s] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
+      s_lof[s] = lo;
       rmax = fmaxf(rmax, hi - lo);
       sa += fmax(fabs((double)lo), fabs((double)hi));
     }
@@ -236,36 +267,58 @@ __global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
     const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
     const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
     const bool ok_scale = (p.scale > 0.f) && isfinite(p.scale) && isfinite(sa);
-    s_inv[g] = rmax > 0.f ? (float)qmax / rmax : 0.f;
+    s_inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
     p.margin[(int64_t)u * GT + g] = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
   }
   __syncthreads();
-  float* tex = p.texact + (int64_t)u * GT * CS * 256;
+  // 16-bit lane of head g inside an entry: GT <= 2 -> u32 entry, lane g;
+  // GT = 4 -> {h0|h2, h1|h3}; GT = 8 -> {h0|h2, h1|h3, h4|h6, h5|h7}.
+  const int lane16 = (GT <= 2) ? g : ((g >> 2) * 4 + (g & 1) * 2 + ((g & 2) >> 1));
+  uint16_t* img = reinterpret_cast<uint16_t*>(p.qimg + (int64_t)u * p.qimg_bytes);
+  float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
+  const float inv = s_inv;
 #pragma unroll
   for (int i = 0; i < SPT; ++i) {
-    const int s = half + 2 * i;
+    const int s = grp + i * groups;
     if (s >= M) continue;
-    uint32_t c[GT];
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      tex[(g * CS + s) * 256 + j] = tv[g][i];
-      float x = __fmul_rn(__fsub_rn(tv[g][i], s_lof[g * CS + s]), s_inv[g]);
+    // entries j >= kpad (never touched by the stream for valid codes) hold T = 0
+    for (int jj = j; jj < 256; jj += kpad) {
+      const float t = (jj == j) ? tv[i] : 0.f;
+      if (jj == j) tex[s * 256 + jj] = t;
+      else tex[s * 256 + jj] = 0.f;
+      float x = __fmul_rn(__fsub_rn(t, s_lof[s]), inv);
       x = fminf(fmaxf(rintf(x), 0.f), (float)qmax);
-      c[g] = (uint32_t)x;
-    }
-    for (int copy = 0; copy < Q::NC; ++copy) {
-      const int e = (Q::rb_of(s) * 256 + j) * Q::COLS + copy * CS + (s % Q::COLS);
-      if constexpr (GT == 1) reinterpret_cast<uint32_t*>(img)[e] = c[0];
-      else if constexpr (GT == 2) reinterpret_cast<uint32_t*>(img)[e] = c[0] | (c[1] << 16);
-      else if constexpr (GT == 4) reinterpret_cast<uint2*>(img)[e] = make_uint2(c[0] | (c[2] << 16), c[1] | (c[3] << 16));
-      else
-        reinterpret_cast<uint4*>(img)[e] = make_uint4(c[0] | (c[2] << 16), c[1] | (c[3] << 16),
-                                                      c[4] | (c[6] << 16), c[5] | (c[7] << 16));
+      const uint16_t code = (uint16_t)x;
+      for (int copy = 0; copy < Q::NC; ++copy) {
+        const int e = (Q::rb_of(s) * 256 + jj) * Q::COLS + copy * CS + (s % Q::COLS);
+        if constexpr (GT == 1) reinterpret_cast<uint32_t*>(img)[e] = code;   // upper lane stays zero
+        else img[(int64_t)e * (Q::EW / 2) + lane16] = code;
+      }
     }
   }
-  __syncthreads();
-  uint4* gimg = reinterpret_cast<uint4*>(p.qimg + (int64_t)u * p.qimg_bytes);
-  for (int i = tid; i < Q::BYTES / 16; i += K5_THREADS) gimg[i] = reinterpret_cast<const uint4*>(img)[i];
+  // padded subspaces s in [M, CS) contribute nothing: zero their entries once
+  if (g == 0 && M < CS) {
+    for (int i = tid; i < (CS - M) * 256; i += blockDim.x) {
+      const int s = M + i / 256, jj = i % 256;
+      for (int copy = 0; copy < Q::NC; ++copy) {
+        const int e = (Q::rb_of(s) * 256 + jj) * Q::COLS + copy * CS + (s % Q::COLS);
+        for (int l = 0; l < Q::EW / 2; ++l) img[(int64_t)e * (Q::EW / 2) + l] = 0;
+      }
+    }
+  }
+}
+
+template <int CS, int GT>
+__global__ void __launch_bounds__(K5_THREADS) k5_tables(Cdc03P p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  pdl_launch_dependents();
+  switch (p.sd) {
+    case 4: k5_body<CS, GT, 4>(p, smem); break;
+    case 8: k5_body<CS, GT, 8>(p, smem); break;
+    case 16: k5_body<CS, GT, 16>(p, smem); break;
+    case 32: k5_body<CS, GT, 32>(p, smem); break;
+    default: dev_flag(HOKV_ERR_DEVICE_INPUT);
+  }
 }
 
 // ===========================================================================
@@ -758,28 +811,54 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     }
     __syncthreads();
     const int n_listed = s_off[p.n_chunks];
-    // listed candidates: index + code row written by the candidate stage
-    for (int base = 0; base < n_listed; base += K7_THREADS) {
-      if (s_n + K7_THREADS > K7_CAP) {
+    // listed candidates: index + code row written by the candidate stage, up to
+    // RPT per thread loaded together (one memory round trip per pass)
+    constexpr int RPT = 4;
+    for (int base = 0; base < n_listed; base += K7_THREADS * RPT) {
+      if (s_n + K7_THREADS * RPT > K7_CAP) {
         select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
         if (tid == 0) s_n = min(s_n, cr.kp);
         __syncthreads();
       }
-      const int i = base + tid;
-      if (i < n_listed) {
-        int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= i < s_off[c + 1]
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (s_off[mid] <= i) lo = mid; else hi = mid - 1;
+      uint32_t tok[RPT], cw[RPT][8];
+      bool ok[RPT];
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        const int i = base + r * K7_THREADS + tid;
+        ok[r] = i < n_listed;
+        tok[r] = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) cw[r][w] = 0;
+        if (ok[r]) {
+          int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= i < s_off[c + 1]
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_off[mid] <= i) lo = mid; else hi = mid - 1;
+          }
+          const int64_t e = (cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (i - s_off[lo]);
+          tok[r] = p.cand_idx[e];
+          const uint8_t* row = p.cand_code + e * p.CS;
+          if (p.CS == 16) {
+            const uint4 v = *reinterpret_cast<const uint4*>(row);
+            cw[r][0] = v.x; cw[r][1] = v.y; cw[r][2] = v.z; cw[r][3] = v.w;
+          } else if (p.CS == 8) {
+            const uint2 v = *reinterpret_cast<const uint2*>(row);
+            cw[r][0] = v.x; cw[r][1] = v.y;
+          } else if (p.CS == 4) {
+            cw[r][0] = *reinterpret_cast<const uint32_t*>(row);
+          } else {
+            const uint4 v = *reinterpret_cast<const uint4*>(row), v2 = *reinterpret_cast<const uint4*>(row + 16);
+            cw[r][0] = v.x; cw[r][1] = v.y; cw[r][2] = v.z; cw[r][3] = v.w;
+            cw[r][4] = v2.x; cw[r][5] = v2.y; cw[r][6] = v2.z; cw[r][7] = v2.w;
+          }
         }
-        const int c = lo;
-        const int slot = i - s_off[c];
-        const int64_t e = (cbase_idx + (int64_t)c * p.GT + g) * CAND_MAX + slot;
-        const uint32_t t = p.cand_idx[e];
-        const uint8_t* row = p.cand_code + e * p.CS;
+      }
+#pragma unroll
+      for (int r = 0; r < RPT; ++r) {
+        if (!ok[r]) continue;
         float sum = 0.f;
-        for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + row[s]]);
-        keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), t);
+        for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + ((cw[r][s >> 2] >> (8 * (s & 3))) & 0xffu)]);
+        keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), tok[r]);
       }
       __syncthreads();
     }

@@ -44,7 +44,9 @@ static inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<u
 // calls made later (e.g. inside CUDA-graph capture) issue no attribute change.
 template <typename K>
 static int ensure_smem(K kernel, size_t bytes) {
-  if (bytes <= 48 * 1024) return HOKV_OK;
+  // Static plus dynamic shared memory above 48 KB needs the opt-in even when
+  // the dynamic part alone is below it, so raise the limit for any request.
+  if (bytes == 0) return HOKV_OK;
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, size_t> done;
   int dev = 0;
@@ -72,7 +74,10 @@ static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
-  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // do not leave the error for the next call to report
+    return fail(HOKV_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  }
   return check_launch(what);
 }
 
@@ -84,9 +89,9 @@ static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   constexpr int TPTM = GT == 8 ? 8 : 16;
   if (p.chunk > TPTM * K6_THREADS || (size_t)p.chunk * CS > 64 * 1024)
     return fail(HOKV_ERR_INVALID, "cdc03: chunk %d too large for this variant", p.chunk);
-  const size_t sm5 = Q::BYTES + 65536 + (size_t)GT * p.D * 4;
+  const size_t sm5 = (size_t)p.M * stage_rows(p.slots, p.M * p.sd) * p.sd * 4;
   if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
-  k5_tables<CS, GT><<<(unsigned)(p.B * p.Hkv), K5_THREADS, sm5, st>>>(p);
+  k5_tables<CS, GT><<<dim3((unsigned)(p.B * p.Hkv), (unsigned)GT), K5_THREADS, sm5, st>>>(p);
   if (int e = check_launch("k5_tables")) return e;
   const size_t sm6 = Q::BYTES + (size_t)p.chunk * CS + (size_t)GT * REFINE_BINS * 4;
   if (int e = ensure_smem(k6_candidates<CS, GT, TPTM>, sm6)) return e;
@@ -443,6 +448,13 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
   const int units = a->batch * a->kv_heads;
   pl->GT = gt_of(a->q_per_kv);
   HOKV_REQUIRE(!(pl->GT == 8 && a->code_bytes > 16), "cdc03: q_per_kv > 4 needs code_bytes <= 16");
+  {
+    const int sd = a->sub_dim > 0 ? a->sub_dim : a->head_dim / a->n_subspaces;
+    if (!(sd == 4 || sd == 8 || sd == 16 || sd == 32))
+      return fail(HOKV_ERR_UNSUPPORTED, "cdc03: sub_dim %d not in {4, 8, 16, 32}", sd);
+    if (a->lut_order != HOKV_DOT_GEMV)
+      return fail(HOKV_ERR_UNSUPPORTED, "cdc03: sub-tables use the GEMV dot order (lut_order = %d)", a->lut_order);
+  }
   const int64_t chunk_max = std::min<int64_t>(pl->GT == 8 ? 2048 : K6_CHUNK_MAX, 65536 / a->code_bytes);
   const int target = 296;  // two resident K6 CTAs per SM on 148 SMs
   int nct = std::max(1, target / units);
