@@ -8,10 +8,14 @@
 //      floor(65535 / M) levels packed in 16-bit lanes, laid out so that every
 //      shared-memory lookup of K6 is bank-conflict free.
 //   K6 k6_candidates  grid (chunks, B*H_kv): streams the uint8 PQ codes of one
-//      chunk of cold tokens (prefetched while K5 runs), sums quantised table
-//      entries per token in integer lanes, finds a lower bound of the chunk's
-//      k'-th largest approximate score and emits every token whose score lies
-//      within the proven error band of it (index + code row).
+//      2048-token chunk of cold tokens straight into registers (the first half
+//      is loaded while K5 runs), sums quantised table entries per token in
+//      integer lanes, finds a lower bound of the k'-th largest approximate
+//      score and emits every token whose score lies within the proven error
+//      band of it (index + code row).  Up to 8 chunks of one (sequence, KV
+//      head) form a thread-block cluster and pool their score histograms
+//      through distributed shared memory, so the bound is the unit's own;
+//      longer contexts use each chunk's own (a looser, still valid bound).
 //   K7 k7_select_attend  grid (B*H_kv*G): attends the hot window before it
 //      waits for K6, then rescores the candidates exactly in the reference's
 //      summation order, selects sinks + top-(k - sinks) (ties to the lower
@@ -28,7 +32,7 @@ namespace hokv {
 
 constexpr int K5_THREADS = 256;
 constexpr int K6_THREADS = 256;
-constexpr int K6_CHUNK_MAX = 4096;   // tokens per K6 CTA (16 per thread)
+
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
 constexpr int K7_CAP = 2048;         // key buffer of the exact selection
@@ -322,15 +326,87 @@ __global__ void __launch_bounds__(K5_THREADS) k5_tables(Cdc03P p) {
 }
 
 // ===========================================================================
-// K6: candidate stream, grid (chunks, B*H_kv), 256 threads.
+// K6: candidate stream, grid (chunks, B*H_kv), 256 threads, 8 tokens per
+// thread.  With CL, the chunks of one (b, KV head) form a thread-block
+// cluster and exchange score histograms through distributed shared memory,
+// so the threshold is the unit-wide k'-th score; without it, the chunk's own.
 // ===========================================================================
-template <int CS, int GT, int TPTM>
-__global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
+constexpr int K6_TPT = 8;
+constexpr int K6_CHUNK = K6_THREADS * K6_TPT;   // 2048 tokens
+constexpr int K6_CLUSTER_MAX = 8;
+
+template <int GT>
+__device__ __forceinline__ void scan_top(const uint32_t (&bins)[16], int per, uint32_t kp, int lane, int& bstar,
+                                         uint32_t& above_out) {
+  // bins[i] holds bin lane*per + i.  Finds the largest bin b such that the
+  // count of items in bins >= b reaches kp (bstar = -1 if the total is < kp).
+  uint32_t ls = 0;
+  for (int i = 0; i < per; ++i) ls += bins[i];
+  uint32_t suf = ls;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += t;
+  }
+  const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
+  bstar = -1;
+  above_out = 0;
+  if (ball != 0u) {
+    const int lstar = 31 - __clz((int)ball);
+    const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
+    int bs = -1;
+    if (lane == lstar) {
+      uint32_t cum = above;
+      for (int i = per - 1; i >= 0; --i) {
+        cum += bins[i];
+        if (cum >= kp) { bs = lane * per + i; break; }
+      }
+    }
+    bstar = __shfl_sync(0xffffffffu, bs, lstar);
+  }
+}
+
+// Sum the NW-word histograms of all CTAs of the cluster (2..8 CTAs) into
+// every CTA's `hist`: rank r reduces slice r with coalesced 16-byte reads of
+// distributed shared memory into `red`, then every rank gathers the slices.
+// `red` holds ceil(NW / 4 / ranks) 16-byte words (NW / 2 words at most).
+// After return, no CTA reads another's `hist`, but it may still read `red`.
+template <int NW>
+__device__ __forceinline__ void pool_cluster(uint32_t* hist, uint32_t* red) {
+  cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+  const int nr = (int)cl.num_blocks(), me = (int)cl.block_rank();
+  constexpr int NV = NW / 4;
+  const int per = (NV + nr - 1) / nr;
+  cl.sync();   // every CTA's histogram is complete
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const int v = me * per + i;
+    if (v >= NV) break;
+    uint4 acc = make_uint4(0u, 0u, 0u, 0u);
+    for (int rk = 0; rk < nr; ++rk) {
+      const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(hist, (unsigned)rk))[v];
+      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+    }
+    reinterpret_cast<uint4*>(red)[i] = acc;
+  }
+  cl.sync();   // all slices reduced: `hist` is no longer read remotely
+  for (int v = threadIdx.x; v < NV; v += blockDim.x) {
+    const int rk = v / per, i = v - rk * per;
+    reinterpret_cast<uint4*>(hist)[v] = reinterpret_cast<const uint4*>(cl.map_shared_rank(red, (unsigned)rk))[i];
+  }
+  __syncthreads();
+}
+
+// Resident CTAs per SM: 4 (64 registers) unless the score lanes need more.
+template <int CS, int GT>
+constexpr int k6_min_blocks() { return ((GT == 8 && CS >= 16) || (CS == 32 && GT >= 4)) ? 3 : 4; }
+
+template <int CS, int GT, bool CL>
+__global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candidates(Cdc03P p) {
   using Q = QGeo<CS, GT>;
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* qlut = smem;                                              // Q::BYTES
-  unsigned char* scodes = smem + Q::BYTES;                                 // chunk * CS
-  uint32_t* hist = reinterpret_cast<uint32_t*>(scodes + p.chunk * CS);     // [GT][REFINE_BINS]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES);           // [GT][REFINE_BINS]
+  [[maybe_unused]] uint32_t* red = hist + GT * REFINE_BINS;               // CL: [GT * REFINE_BINS / 2]
   __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_alb[GT], s_sh2[GT];
 
   pdl_launch_dependents();
@@ -338,24 +414,34 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   const int b = u / p.Hkv, h = u - b * p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ColdRange cr = cold_range(p, b);
-  const int lo_t = max(c * p.chunk, cr.sink), hi_t = min((c + 1) * p.chunk, cr.Sc);
   int* cnt_out = p.cand_cnt + ((int64_t)u * p.n_chunks + c) * GT;
-  if (cr.k >= cr.Sc || cr.kp <= 0 || lo_t >= hi_t) {
+  if (cr.k >= cr.Sc || cr.kp <= 0) {      // the same for every chunk of the unit
+    if (tid < GT) cnt_out[tid] = 0;
+    return;
+  }
+  const int t0 = c * K6_CHUNK;
+  const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
+  if (!CL && lo_t >= hi_t) {
     if (tid < GT) cnt_out[tid] = 0;
     return;
   }
   const int M = p.M;
-  // ---- prefetch this chunk's codes (independent of the tables) -------------
-  const int t0 = c * p.chunk;
-  const int ntok = min(p.chunk, cr.Sc - t0);
-  const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh + (int64_t)t0 * CS;
-  {
-    const int n16 = (ntok * CS + 15) / 16;
-    for (int i = tid; i < n16; i += K6_THREADS) cp_async16(scodes + i * 16, gcodes + (int64_t)i * 16);
+  const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
+
+  // ---- first half of this thread's codes, loaded before waiting for K5 -----
+  constexpr int HT = K6_TPT / 2;
+  uint32_t w[HT][Q::W];
+#pragma unroll
+  for (int it = 0; it < HT; ++it) {
+    const int t = t0 + it * K6_THREADS + tid;
+    if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
+    else {
+#pragma unroll
+      for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
+    }
   }
   for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
   if (tid < GT) s_cnt[tid] = 0;
-  // ---- tables from K5 --------------------------------------------------------
   pdl_wait();
   {
     const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
@@ -373,86 +459,75 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
     const int s = (uu + r) % CS;
     colidx[uu] = Q::rb_of(s) * 256 * Q::COLS + Q::col_of(lane, s);
   }
-  uint32_t accs[TPTM][Q::NACC];
+  uint32_t accs[K6_TPT][Q::NACC];
   int mxv[GT];
 #pragma unroll
   for (int g = 0; g < GT; ++g) mxv[g] = -1;
-  const int tpt = p.chunk / K6_THREADS;
 #pragma unroll
-  for (int it = 0; it < TPTM; ++it) {
+  for (int half = 0; half < 2; ++half) {
+    if (half == 1) {
 #pragma unroll
-    for (int a = 0; a < Q::NACC; ++a) accs[it][a] = 0;
-    if (it >= tpt) continue;
-    const int lt = it * K6_THREADS + tid;
-    const int t = t0 + lt;
-    uint32_t w[Q::W];
-    if constexpr (Q::W == 1) w[0] = *reinterpret_cast<const uint32_t*>(scodes + lt * CS);
-    else if constexpr (Q::W == 2) { const uint2 v = *reinterpret_cast<const uint2*>(scodes + lt * CS); w[0] = v.x; w[1] = v.y; }
-    else {
+      for (int it = 0; it < HT; ++it) {
+        const int t = t0 + (HT + it) * K6_THREADS + tid;
+        if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
+        else {
 #pragma unroll
-      for (int q4 = 0; q4 < Q::W / 4; ++q4) {
-        const uint4 v = *reinterpret_cast<const uint4*>(scodes + lt * CS + q4 * 16);
-        w[q4 * 4 + 0] = v.x; w[q4 * 4 + 1] = v.y; w[q4 * 4 + 2] = v.z; w[q4 * 4 + 3] = v.w;
+          for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
+        }
       }
     }
-    rotate_bytes<Q::W>(w, r);
 #pragma unroll
-    for (int uu = 0; uu < CS; ++uu) {
-      const uint32_t byte = (w[uu >> 2] >> (8 * (uu & 3))) & 0xffu;
-      const int e = colidx[uu] + (int)byte * Q::COLS;
-      if constexpr (Q::EW == 4) {
-        accs[it][0] += reinterpret_cast<const uint32_t*>(qlut)[e];
-      } else if constexpr (Q::EW == 8) {
-        const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
-        accs[it][0] += x.x; accs[it][1] += x.y;
-      } else {
-        const uint4 x = reinterpret_cast<const uint4*>(qlut)[e];
-        accs[it][0] += x.x; accs[it][1] += x.y; accs[it][2] += x.z; accs[it][3] += x.w;
+    for (int it = 0; it < HT; ++it) {
+      const int ti = half * HT + it;
+      const int t = t0 + ti * K6_THREADS + tid;
+#pragma unroll
+      for (int a = 0; a < Q::NACC; ++a) accs[ti][a] = 0;
+      rotate_bytes<Q::W>(w[it], r);
+#pragma unroll
+      for (int uu = 0; uu < CS; ++uu) {
+        const uint32_t byte = (w[it][uu >> 2] >> (8 * (uu & 3))) & 0xffu;
+        const int e = colidx[uu] + (int)byte * Q::COLS;
+        if constexpr (Q::EW == 4) {
+          accs[ti][0] += reinterpret_cast<const uint32_t*>(qlut)[e];
+        } else if constexpr (Q::EW == 8) {
+          const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
+          accs[ti][0] += x.x; accs[ti][1] += x.y;
+        } else {
+          const uint4 x = reinterpret_cast<const uint4*>(qlut)[e];
+          accs[ti][0] += x.x; accs[ti][1] += x.y; accs[ti][2] += x.z; accs[ti][3] += x.w;
+        }
       }
-    }
-    if (t >= lo_t && t < hi_t) {
+      if (t >= lo_t && t < hi_t) {
 #pragma unroll
-      for (int g = 0; g < GT; ++g) mxv[g] = max(mxv[g], approx_of<GT>(accs[it], g));
+        for (int g = 0; g < GT; ++g) mxv[g] = max(mxv[g], approx_of<GT>(accs[ti], g));
+      }
     }
   }
 
   // ---- threshold: coarse (per-thread maxima), then refined (all tokens) -----
+  // Coarse histograms hold 256 bins per head, refined ones REFINE_BINS.
   const int maxv = M * qmax_for(M);
   int sh = 0;
   while ((maxv >> sh) > 255) ++sh;
 #pragma unroll
   for (int g = 0; g < GT; ++g)
-    if (mxv[g] >= 0) atomicAdd(&hist[g * REFINE_BINS + (mxv[g] >> sh)], 1u);
-  __syncthreads();
+    if (mxv[g] >= 0) atomicAdd(&hist[g * 256 + (mxv[g] >> sh)], 1u);
   const uint32_t kp = (uint32_t)cr.kp;
+  if constexpr (CL) pool_cluster<GT * 256>(hist, red); else __syncthreads();
   if (warp < GT) {
     const int g = warp;
-    const uint32_t* hg = hist + g * REFINE_BINS;
-    uint32_t ls = 0;
+    uint32_t bins[16];
     int top = -1;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) { const uint32_t v = hg[lane * 8 + i]; ls += v; if (v) top = lane * 8 + i; }
-    top = __reduce_max_sync(0xffffffffu, top + 1) - 1;
-    uint32_t suf = ls;
+    for (int i = 0; i < 8; ++i) bins[i] = hist[g * 256 + lane * 8 + i];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-      if (lane + o < 32) suf += t;
-    }
-    const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
+    for (int i = 0; i < 8; ++i) if (bins[i]) top = lane * 8 + i;
+    top = __reduce_max_sync(0xffffffffu, top + 1) - 1;
+    int bstar;
+    uint32_t above;
+    scan_top<GT>(bins, 8, kp, lane, bstar, above);
     int alb = -1, sh2 = 0;
-    if (ball != 0u) {
-      const int lstar = 31 - __clz((int)ball);
-      const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
-      int bstar = -1;
-      if (lane == lstar) {
-        uint32_t cum = above;
-        for (int i = 7; i >= 0; --i) {
-          cum += hg[lane * 8 + i];
-          if (cum >= kp) { bstar = lane * 8 + i; break; }
-        }
-      }
-      bstar = __shfl_sync(0xffffffffu, bstar, lstar);
+    if (bstar >= 0) {
       alb = bstar << sh;
       const int span = ((top + 1) << sh) - alb;
       while ((span >> sh2) >= REFINE_BINS) ++sh2;
@@ -463,64 +538,44 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
   for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
   __syncthreads();
 #pragma unroll
-  for (int it = 0; it < TPTM; ++it) {
-    if (it >= tpt) break;
-    const int t = t0 + it * K6_THREADS + tid;
+  for (int ti = 0; ti < K6_TPT; ++ti) {
+    const int t = t0 + ti * K6_THREADS + tid;
     if (t < lo_t || t >= hi_t) continue;
 #pragma unroll
     for (int g = 0; g < GT; ++g) {
-      const int a = approx_of<GT>(accs[it], g), alb = s_alb[g];
+      const int a = approx_of<GT>(accs[ti], g), alb = s_alb[g];
       if (alb >= 0 && a >= alb) atomicAdd(&hist[g * REFINE_BINS + ((a - alb) >> s_sh2[g])], 1u);
     }
   }
-  __syncthreads();
+  if constexpr (CL) pool_cluster<GT * REFINE_BINS>(hist, red); else __syncthreads();
   if (warp < GT) {
     const int g = warp;
-    const uint32_t* hg = hist + g * REFINE_BINS;
     constexpr int PER = REFINE_BINS / 32;
-    uint32_t ls = 0;
+    uint32_t bins[16];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) ls += hg[lane * PER + i];
-    uint32_t suf = ls;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-      if (lane + o < 32) suf += t;
-    }
-    const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
+    for (int i = 0; i < PER; ++i) bins[i] = hist[g * REFINE_BINS + lane * PER + i];
+    int bstar;
+    uint32_t above;
+    scan_top<GT>(bins, PER, kp, lane, bstar, above);
     int thr = -(1 << 30);
-    if (s_alb[g] >= 0 && ball != 0u) {
-      const int lstar = 31 - __clz((int)ball);
-      const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
-      int bstar = -1;
-      if (lane == lstar) {
-        uint32_t cum = above;
-        for (int i = PER - 1; i >= 0; --i) {
-          cum += hg[lane * PER + i];
-          if (cum >= kp) { bstar = lane * PER + i; break; }
-        }
-      }
-      bstar = __shfl_sync(0xffffffffu, bstar, lstar);
-      thr = s_alb[g] + (bstar << s_sh2[g]) - s_margin[g];
-    }
+    if (s_alb[g] >= 0 && bstar >= 0) thr = s_alb[g] + (bstar << s_sh2[g]) - s_margin[g];
     if (lane == 0) s_thr[g] = (s_margin[g] >= (1 << 30)) ? -(1 << 30) : thr;
   }
-  __syncthreads();
+  // the other CTAs of the cluster may still be gathering from `red`
+  if constexpr (CL) cooperative_groups::this_cluster().sync(); else __syncthreads();
 
   // ---- emit candidates: token index and its code row --------------------------
   const int64_t cbase_idx = ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
   uint32_t* cand = p.cand_idx + cbase_idx;
   uint8_t* ccode = p.cand_code + cbase_idx * CS;
 #pragma unroll
-  for (int it = 0; it < TPTM; ++it) {
-    if (it >= tpt) break;
-    const int lt = it * K6_THREADS + tid;
-    const int t = t0 + lt;
+  for (int ti = 0; ti < K6_TPT; ++ti) {
+    const int t = t0 + ti * K6_THREADS + tid;
     const bool valid = t >= lo_t && t < hi_t;
 #pragma unroll
     for (int g = 0; g < GT; ++g) {
       if (g >= p.G) break;   // uniform across the block
-      const bool pred = valid && approx_of<GT>(accs[it], g) >= s_thr[g];
+      const bool pred = valid && approx_of<GT>(accs[ti], g) >= s_thr[g];
       const unsigned m = __ballot_sync(0xffffffffu, pred);
       if (m) {
         const int leader = __ffs(m) - 1;
@@ -530,10 +585,11 @@ __global__ void __launch_bounds__(K6_THREADS, 2) k6_candidates(Cdc03P p) {
         const int slot = basep + __popc(m & ((1u << lane) - 1u));
         if (pred && slot < CAND_MAX) {
           cand[g * CAND_MAX + slot] = (uint32_t)t;
-          uint8_t* dst = ccode + ((int64_t)g * CAND_MAX + slot) * CS;
+          uint32_t cw[Q::W];
+          load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
+          uint32_t* dst = reinterpret_cast<uint32_t*>(ccode + ((int64_t)g * CAND_MAX + slot) * CS);
 #pragma unroll
-          for (int q4 = 0; q4 < CS; q4 += 4)
-            *reinterpret_cast<uint32_t*>(dst + q4) = *reinterpret_cast<const uint32_t*>(scodes + lt * CS + q4);
+          for (int i = 0; i < Q::W; ++i) dst[i] = cw[i];
         }
       }
     }

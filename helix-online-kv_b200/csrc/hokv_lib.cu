@@ -61,18 +61,29 @@ static int ensure_smem(K kernel, size_t bytes) {
   return HOKV_OK;
 }
 
+// Programmatic (PDL) launch; cluster_x > 0 also groups cluster_x consecutive
+// blocks along x into one thread-block cluster.
 template <typename K>
-static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st, const Cdc03P& p, const char* what) {
+static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st, const Cdc03P& p, const char* what,
+                      int cluster_x = 0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = sm;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (cluster_x > 0) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();  // do not leave the error for the next call to report
@@ -86,17 +97,22 @@ static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t s
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
-  constexpr int TPTM = GT == 8 ? 8 : 16;
-  if (p.chunk > TPTM * K6_THREADS || (size_t)p.chunk * CS > 64 * 1024)
-    return fail(HOKV_ERR_INVALID, "cdc03: chunk %d too large for this variant", p.chunk);
+  if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
   const size_t sm5 = (size_t)p.M * stage_rows(p.slots, p.M * p.sd) * p.sd * 4;
   if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
   k5_tables<CS, GT><<<dim3((unsigned)(p.B * p.Hkv), (unsigned)GT), K5_THREADS, sm5, st>>>(p);
   if (int e = check_launch("k5_tables")) return e;
-  const size_t sm6 = Q::BYTES + (size_t)p.chunk * CS + (size_t)GT * REFINE_BINS * 4;
-  if (int e = ensure_smem(k6_candidates<CS, GT, TPTM>, sm6)) return e;
-  return launch_pdl(k6_candidates<CS, GT, TPTM>, dim3((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv)),
-                    dim3(K6_THREADS), sm6, st, p, "k6_candidates");
+  const size_t sm6 = Q::BYTES + (size_t)GT * REFINE_BINS * 4;
+  const dim3 grid6((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
+  if (p.n_chunks >= 2 && p.n_chunks <= K6_CLUSTER_MAX) {
+    // one cluster per (sequence, KV head): a unit-wide threshold
+    const size_t smc = sm6 + (size_t)GT * REFINE_BINS * 2;
+    if (int e = ensure_smem(k6_candidates<CS, GT, true>, smc)) return e;
+    return launch_pdl(k6_candidates<CS, GT, true>, grid6, dim3(K6_THREADS), smc, st, p, "k6_candidates",
+                      p.n_chunks);
+  }
+  if (int e = ensure_smem(k6_candidates<CS, GT, false>, sm6)) return e;
+  return launch_pdl(k6_candidates<CS, GT, false>, grid6, dim3(K6_THREADS), sm6, st, p, "k6_candidates");
 }
 
 static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
@@ -455,14 +471,8 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
     if (a->lut_order != HOKV_DOT_GEMV)
       return fail(HOKV_ERR_UNSUPPORTED, "cdc03: sub-tables use the GEMV dot order (lut_order = %d)", a->lut_order);
   }
-  const int64_t chunk_max = std::min<int64_t>(pl->GT == 8 ? 2048 : K6_CHUNK_MAX, 65536 / a->code_bytes);
-  const int target = 296;  // two resident K6 CTAs per SM on 148 SMs
-  int nct = std::max(1, target / units);
-  int64_t chunk = cdiv(std::max<int64_t>(cold_cap, 1), nct);
-  chunk = cdiv(chunk, K6_THREADS) * K6_THREADS;
-  chunk = std::min<int64_t>(std::max<int64_t>(chunk, K6_THREADS), chunk_max);
-  pl->chunk = (int)chunk;
-  pl->n_chunks = (int)std::max<int64_t>(1, cdiv(cold_cap, chunk));
+  pl->chunk = K6_CHUNK;
+  pl->n_chunks = (int)std::max<int64_t>(1, cdiv(cold_cap, K6_CHUNK));
   if (pl->n_chunks > MAX_CHUNKS)
     return fail(HOKV_ERR_UNSUPPORTED, "cdc03: capacity %lld needs %d chunks > %d", (long long)a->capacity,
                 pl->n_chunks, MAX_CHUNKS);
