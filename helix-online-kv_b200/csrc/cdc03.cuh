@@ -38,7 +38,6 @@ constexpr int K7_THREADS = 256;
 constexpr int K7_CAP = 2048;         // key buffer of the exact selection
 constexpr int TOPK_MAX = 1024;       // largest top_k with k < S_c
 constexpr int MAX_CHUNKS = 512;      // K6 chunks per (sequence, KV head)
-constexpr int REFINE_BINS = 512;
 
 struct Cdc03P {
   int B, Hkv, G, D, M, sd, CS, slots, top_k, sink, hot;
@@ -54,7 +53,8 @@ struct Cdc03P {
   const int* seq_len;
   int* sel_idx; float* sel_score; int* sel_count;
   // workspace
-  uint32_t* cand_idx; int* cand_cnt; uint8_t* cand_code;
+  uint64_t* cand_key;     // [units][chunks][GT][CAND_MAX] selection keys of listed candidates (K6 -> K7)
+  int* cand_cnt;          // [units][chunks][GT]   listed count, -1 when the list overflowed
   unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (K5 -> K6)
   float* texact;          // [units][GT][CS][256]    exact sub-tables (K5 -> K7)
   int* margin;            // [units][GT]             error band in code units (K5 -> K6)
@@ -193,13 +193,46 @@ __device__ __forceinline__ float lut_dot(const float* q, const float* c) {
   return dot_gemv(q, c, SD);
 }
 
+// Quantisation of one head's tables from the per-subspace ranges [lo, hi]
+// (0 included where a subspace has fewer than 256 centroids): a common step
+// delta = max range / qmax, and the error band, in code units, that covers
+// entry rounding (<= 0.5 + fp32 slop) for both tokens of a comparison, the
+// fp32 summation error of the exact scores and ties created by the final
+// scale multiply.  A margin of 2^30 marks a scale that cannot rank.
+struct QuantScale {
+  float inv;
+  int margin;
+};
+__device__ __forceinline__ QuantScale quant_scale(const float* lo, const float* hi, int M, float scale) {
+  const int qmax = qmax_for(M);
+  float rmax = 0.f;
+  double sa = 0.0;
+  for (int s = 0; s < M; ++s) {
+    rmax = fmaxf(rmax, hi[s] - lo[s]);
+    sa += fmax(fabs((double)lo[s]), fabs((double)hi[s]));
+  }
+  const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
+  const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
+  const bool ok_scale = (scale > 0.f) && isfinite(scale) && isfinite(sa);
+  QuantScale r;
+  r.inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
+  r.margin = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
+  return r;
+}
+
+__device__ __forceinline__ uint16_t quant_code(float t, float lo, float inv, int qmax) {
+  float x = __fmul_rn(__fsub_rn(t, lo), inv);
+  x = fminf(fmaxf(rintf(x), 0.f), (float)qmax);
+  return (uint16_t)x;
+}
+
 template <int CS, int GT, int SD>
 __device__ __forceinline__ void k5_body(const Cdc03P& p, unsigned char* smem) {
   using Q = QGeo<CS, GT>;
   float* stage = reinterpret_cast<float*>(smem);               // <= 64 KB
   __shared__ float sq[256];
   __shared__ unsigned s_lo[CS], s_hi[CS];
-  __shared__ float s_lof[CS], s_inv;
+  __shared__ float s_lof[CS], s_hif[CS], s_inv;
   __shared__ int s_k[32], s_kmax;
 
   const int u = blockIdx.x, g = blockIdx.y;
@@ -256,23 +289,15 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, unsigned char* smem) {
   __syncthreads();
   const int qmax = qmax_for(M);
   if (tid == 0) {
-    float rmax = 0.f;
-    double sa = 0.0;
     for (int s = 0; s < M; ++s) {
       float lo = unord_f32(s_lo[s]), hi = unord_f32(s_hi[s]);
       if (s_k[s] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
       s_lof[s] = lo;
-      rmax = fmaxf(rmax, hi - lo);
-      sa += fmax(fabs((double)lo), fabs((double)hi));
+      s_hif[s] = hi;
     }
-    // Error budget in code units: entry rounding (<= 0.5 + fp32 slop) for both
-    // tokens of a comparison, the fp32 summation error of the exact scores and
-    // ties created by the final scale multiply.
-    const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
-    const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
-    const bool ok_scale = (p.scale > 0.f) && isfinite(p.scale) && isfinite(sa);
-    s_inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
-    p.margin[(int64_t)u * GT + g] = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
+    const QuantScale qs = quant_scale(s_lof, s_hif, M, p.scale);
+    s_inv = qs.inv;
+    p.margin[(int64_t)u * GT + g] = qs.margin;
   }
   __syncthreads();
   // 16-bit lane of head g inside an entry: GT <= 2 -> u32 entry, lane g;
@@ -290,9 +315,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, unsigned char* smem) {
       const float t = (jj == j) ? tv[i] : 0.f;
       if (jj == j) tex[s * 256 + jj] = t;
       else tex[s * 256 + jj] = 0.f;
-      float x = __fmul_rn(__fsub_rn(t, s_lof[s]), inv);
-      x = fminf(fmaxf(rintf(x), 0.f), (float)qmax);
-      const uint16_t code = (uint16_t)x;
+      const uint16_t code = quant_code(t, s_lof[s], inv, qmax);
       for (int copy = 0; copy < Q::NC; ++copy) {
         const int e = (Q::rb_of(s) * 256 + jj) * Q::COLS + copy * CS + (s % Q::COLS);
         if constexpr (GT == 1) reinterpret_cast<uint32_t*>(img)[e] = code;   // upper lane stays zero
@@ -327,21 +350,68 @@ __global__ void __launch_bounds__(K5_THREADS) k5_tables(Cdc03P p) {
 
 // ===========================================================================
 // K6: candidate stream, grid (chunks, B*H_kv), 256 threads, 8 tokens per
-// thread.  With CL, the chunks of one (b, KV head) form a thread-block
-// cluster and exchange score histograms through distributed shared memory,
-// so the threshold is the unit-wide k'-th score; without it, the chunk's own.
+// thread.  FUSED (up to 8 chunks per unit): the chunks of one (b, KV head)
+// form a thread-block cluster that builds the unit's tables itself (each CTA
+// one block of subspaces, exchanged through distributed shared memory) and
+// pools its score histograms, so the threshold is the unit-wide k'-th score.
+// Otherwise K5 has built the tables and each chunk uses its own threshold.
 // ===========================================================================
 constexpr int K6_TPT = 8;
 constexpr int K6_CHUNK = K6_THREADS * K6_TPT;   // 2048 tokens
 constexpr int K6_CLUSTER_MAX = 8;
+constexpr int HBINS = 1024;                      // score histogram bins per head
+constexpr int HWORDS = HBINS / 2;                // two 16-bit counters per word
+constexpr int HSHIFT = 6;                        // bin = approx >> 6 (approx <= 65535)
 
-template <int GT>
-__device__ __forceinline__ void scan_top(const uint32_t (&bins)[16], int per, uint32_t kp, int lane, int& bstar,
-                                         uint32_t& above_out) {
-  // bins[i] holds bin lane*per + i.  Finds the largest bin b such that the
-  // count of items in bins >= b reaches kp (bstar = -1 if the total is < kp).
+// Cluster barrier halves (every thread of every CTA of the cluster arrives,
+// then waits, once per phase).  `arrive` releases this thread's earlier
+// shared and global writes to the cluster; `wait` acquires them.
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
+// Sum the NW-word histograms `hist` of the R CTAs of the cluster into every
+// CTA's `full`: rank r adds up slice r (16-byte reads of distributed shared
+// memory) and stores the sum into the `full` of every rank.  Two cluster
+// barrier phases; afterwards no CTA touches another's shared memory.
+template <int NW>
+__device__ __forceinline__ void pool_cluster(const uint32_t* hist, uint32_t* full, int R, int me) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  constexpr int NV = NW / 4;
+  const int per = (NV + R - 1) / R;
+  cluster_arrive();
+  cluster_wait();   // every CTA's histogram is complete
+  for (int i = threadIdx.x; i < per; i += blockDim.x) {
+    const int v = me * per + i;
+    if (v >= NV) break;
+    uint4 acc = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk) {
+      if (rk < R) {
+        const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(const_cast<uint32_t*>(hist), (unsigned)rk))[v];
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+    }
+#pragma unroll
+    for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk)
+      if (rk < R) reinterpret_cast<uint4*>(cl.map_shared_rank(full, (unsigned)rk))[v] = acc;
+  }
+  cluster_arrive();
+  cluster_wait();   // every slice is in every CTA's `full`
+}
+
+// Largest bin b of one head's packed histogram (HWORDS words, bin 2i in the
+// low half of word i) such that at least kp items lie in bins >= b; -1 if
+// the histogram holds fewer than kp items.  One warp; lane L owns bins
+// [32L, 32L + 32).
+__device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane) {
   uint32_t ls = 0;
-  for (int i = 0; i < per; ++i) ls += bins[i];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t w = h[lane * 16 + i];
+    ls += (w & 0xffffu) + (w >> 16);
+  }
   uint32_t suf = ls;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -349,65 +419,96 @@ __device__ __forceinline__ void scan_top(const uint32_t (&bins)[16], int per, ui
     if (lane + o < 32) suf += t;
   }
   const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
-  bstar = -1;
-  above_out = 0;
-  if (ball != 0u) {
-    const int lstar = 31 - __clz((int)ball);
-    const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
-    int bs = -1;
-    if (lane == lstar) {
-      uint32_t cum = above;
-      for (int i = per - 1; i >= 0; --i) {
-        cum += bins[i];
-        if (cum >= kp) { bs = lane * per + i; break; }
-      }
+  if (ball == 0u) return -1;
+  const int lstar = 31 - __clz((int)ball);
+  int bs = -1;
+  if (lane == lstar) {
+    uint32_t cum = suf - ls;
+    for (int i = 15; i >= 0 && bs < 0; --i) {
+      const uint32_t w = h[lane * 16 + i];
+      cum += w >> 16;
+      if (cum >= kp) { bs = lane * 32 + 2 * i + 1; break; }
+      cum += w & 0xffffu;
+      if (cum >= kp) bs = lane * 32 + 2 * i;
     }
-    bstar = __shfl_sync(0xffffffffu, bs, lstar);
   }
-}
-
-// Sum the NW-word histograms of all CTAs of the cluster (2..8 CTAs) into
-// every CTA's `hist`: rank r reduces slice r with coalesced 16-byte reads of
-// distributed shared memory into `red`, then every rank gathers the slices.
-// `red` holds ceil(NW / 4 / ranks) 16-byte words (NW / 2 words at most).
-// After return, no CTA reads another's `hist`, but it may still read `red`.
-template <int NW>
-__device__ __forceinline__ void pool_cluster(uint32_t* hist, uint32_t* red) {
-  cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
-  const int nr = (int)cl.num_blocks(), me = (int)cl.block_rank();
-  constexpr int NV = NW / 4;
-  const int per = (NV + nr - 1) / nr;
-  cl.sync();   // every CTA's histogram is complete
-  for (int i = threadIdx.x; i < per; i += blockDim.x) {
-    const int v = me * per + i;
-    if (v >= NV) break;
-    uint4 acc = make_uint4(0u, 0u, 0u, 0u);
-    for (int rk = 0; rk < nr; ++rk) {
-      const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(hist, (unsigned)rk))[v];
-      acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-    }
-    reinterpret_cast<uint4*>(red)[i] = acc;
-  }
-  cl.sync();   // all slices reduced: `hist` is no longer read remotely
-  for (int v = threadIdx.x; v < NV; v += blockDim.x) {
-    const int rk = v / per, i = v - rk * per;
-    reinterpret_cast<uint4*>(hist)[v] = reinterpret_cast<const uint4*>(cl.map_shared_rank(red, (unsigned)rk))[i];
-  }
-  __syncthreads();
+  return __shfl_sync(0xffffffffu, bs, lstar);
 }
 
 // Resident CTAs per SM: 4 (64 registers) unless the score lanes need more.
 template <int CS, int GT>
 constexpr int k6_min_blocks() { return ((GT == 8 && CS >= 16) || (CS == 32 && GT >= 4)) ? 3 : 4; }
 
-template <int CS, int GT, bool CL>
+// Dot phase of the in-cluster table build: thread j computes entry j of the
+// subspaces [s_begin, s_end) for the GT query heads of the group, stores the
+// exact fp32 value (for the exact rescoring), folds it into the
+// per-(head, subspace) range and keeps the first two subspaces' values in
+// registers for the quantisation.  Row (s, j) of the codebook is at
+// rows + ((s - s_off) * slots + j) * SD.
+template <int GT, int SD>
+__device__ __forceinline__ void lut_dot_row(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
+                                            const int* s_k, int s, unsigned (*s_lo)[32], unsigned (*s_hi)[32],
+                                            float (&tv)[GT]) {
+  const int j = threadIdx.x, lane = j & 31;
+  const bool live = j < s_k[s];
+  float c[SD];
+  const float* row = rows + ((int64_t)(s - s_off) * p.slots + j) * SD;
+#pragma unroll
+  for (int d = 0; d < SD; ++d) c[d] = live ? row[d] : 0.f;
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+    const float t = live ? lut_dot<SD>(sq + g * p.D + s * SD, c) : 0.f;
+    tv[g] = t;
+    p.texact[(((int64_t)u * GT + g) * p.CS + s) * 256 + j] = t;
+    const unsigned o = ord_f32(t);
+    const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
+    if (lane == 0) { atomicMin(&s_lo[g][s], mn); atomicMax(&s_hi[g][s], mx); }
+  }
+}
+
+template <int GT, int SD>
+__device__ __forceinline__ void lut_dots(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
+                                         const int* s_k, int s_begin, int s_end, unsigned (*s_lo)[32],
+                                         unsigned (*s_hi)[32], float (&tv)[2][GT]) {
+  if (s_begin < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin, s_lo, s_hi, tv[0]);
+  if (s_begin + 1 < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin + 1, s_lo, s_hi, tv[1]);
+  for (int s = s_begin + 2; s < s_end; ++s) {
+    float tmp[GT];
+    lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s, s_lo, s_hi, tmp);
+  }
+}
+
+// Quantised entry (EW bytes, GT 16-bit lanes) of subspace sx, row j, into the
+// unit's image in global memory, every copy of the column.
+// 16-bit lane of head g: GT <= 2 -> u32 lane g; GT = 4 -> {h0|h2, h1|h3};
+// GT = 8 -> {h0|h2, h1|h3, h4|h6, h5|h7}.
+template <int CS, int GT>
+__device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, const uint32_t* code) {
+  using Q = QGeo<CS, GT>;
+  uint32_t e32[Q::EW / 4];
+#pragma unroll
+  for (int i = 0; i < Q::EW / 4; ++i) e32[i] = 0u;
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+    const int l16 = (GT <= 2) ? g : ((g >> 2) * 4 + (g & 1) * 2 + ((g & 2) >> 1));
+    e32[l16 >> 1] |= code[g] << (16 * (l16 & 1));
+  }
+  for (int copy = 0; copy < Q::NC; ++copy) {
+    const int e = (Q::rb_of(sx) * 256 + j) * Q::COLS + copy * CS + (sx % Q::COLS);
+    if constexpr (Q::EW == 4) reinterpret_cast<uint32_t*>(img)[e] = e32[0];
+    else if constexpr (Q::EW == 8) reinterpret_cast<uint2*>(img)[e] = make_uint2(e32[0], e32[1]);
+    else reinterpret_cast<uint4*>(img)[e] = make_uint4(e32[0], e32[1], e32[2], e32[3]);
+  }
+}
+
+template <int CS, int GT, bool FUSED>
 __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candidates(Cdc03P p) {
   using Q = QGeo<CS, GT>;
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* qlut = smem;                                              // Q::BYTES
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES);           // [GT][REFINE_BINS]
-  [[maybe_unused]] uint32_t* red = hist + GT * REFINE_BINS;               // CL: [GT * REFINE_BINS / 2]
-  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_alb[GT], s_sh2[GT];
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES);           // [GT][HWORDS]
+  uint32_t* full = FUSED ? hist + GT * HWORDS : hist;                      // [GT][HWORDS] pooled
+  __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_nl[GT];
 
   pdl_launch_dependents();
   const int u = blockIdx.y, c = blockIdx.x;
@@ -421,37 +522,160 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   }
   const int t0 = c * K6_CHUNK;
   const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
-  if (!CL && lo_t >= hi_t) {
+  if (!FUSED && lo_t >= hi_t) {
     if (tid < GT) cnt_out[tid] = 0;
     return;
   }
   const int M = p.M;
   const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
-
-  // ---- first half of this thread's codes, loaded before waiting for K5 -----
   constexpr int HT = K6_TPT / 2;
   uint32_t w[HT][Q::W];
-#pragma unroll
-  for (int it = 0; it < HT; ++it) {
-    const int t = t0 + it * K6_THREADS + tid;
-    if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
-    else {
-#pragma unroll
-      for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
-    }
-  }
-  for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
-  if (tid < GT) s_cnt[tid] = 0;
-  pdl_wait();
-  {
-    const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-    for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
-  }
-  if (tid < GT) s_margin[tid] = p.margin[(int64_t)u * GT + tid];
-  cp_async_wait_all();
-  __syncthreads();
+  [[maybe_unused]] int R = 1, me = 0;
 
-  // ---- quantised scores, kept in registers -----------------------------------
+  if constexpr (FUSED) {
+    // ---- tables built by the cluster: each CTA computes a block of subspaces
+    // (whole 16-byte groups of the image), the ranges go to every CTA through
+    // distributed shared memory, the quantised entries to the unit's image in
+    // global memory, from where every CTA loads the whole image
+    __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
+    __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
+    __shared__ int s_k[32];
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    R = (int)cl.num_blocks();
+    me = (int)cl.block_rank();
+    cluster_arrive_relaxed();   // phase A: this CTA runs
+    {   // codes of this chunk into L2 while the tables are built
+      const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
+      for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
+    }
+    constexpr int GS = 16 / Q::EW;                 // subspaces per 16-byte group
+    const int ngm = (M + GS - 1) / GS;             // groups holding real subspaces
+    const int grp0 = me * ngm / R, grp1 = (me + 1) * ngm / R;
+    const int s_begin = grp0 * GS, s_end = min(grp1 * GS, M);
+    const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+    // own codebook rows into shared memory (the image space is free until the
+    // image is loaded), with the queries
+    const int64_t blk = (int64_t)max(0, s_end - s_begin) * p.slots * p.sd;   // floats
+    const bool staged = blk * 4 <= Q::BYTES;
+    if (staged) {
+      const float* src = cbase + (int64_t)s_begin * p.slots * p.sd;
+      for (int64_t i = tid; i < blk / 4; i += K6_THREADS) cp_async16(qlut + i * 16, src + i * 4);
+    }
+    float* sq = reinterpret_cast<float*>(hist);   // [GT][D], dead before the histograms
+    for (int i = tid; i < GT * p.D; i += K6_THREADS) {
+      const int g = i / p.D, d = i - g * p.D;
+      sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
+    }
+    if (tid < M) {
+      const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+      s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
+    }
+    if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
+    cp_async_wait_all();
+    __syncthreads();
+    float tv[2][GT];
+    const float* rows = staged ? reinterpret_cast<const float*>(qlut) : cbase;
+    const int s_off = staged ? s_begin : 0;
+    switch (p.sd) {
+      case 4: lut_dots<GT, 4>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 8: lut_dots<GT, 8>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 16: lut_dots<GT, 16>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 32: lut_dots<GT, 32>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      default: dev_flag(HOKV_ERR_DEVICE_INPUT);
+    }
+    __syncthreads();
+    cluster_wait();             // phase A: every CTA of the cluster runs
+    if (tid < GT * 32) {        // own ranges into every CTA
+      const int g = tid / 32, sx = tid % 32;
+      if (sx >= s_begin && sx < s_end) {
+        float lo = unord_f32(s_lo[g][sx]), hi = unord_f32(s_hi[g][sx]);
+        if (s_k[sx] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
+        for (int rk = 0; rk < R; ++rk) {
+          cl.map_shared_rank(&f_lo[0][0], (unsigned)rk)[g * 32 + sx] = lo;
+          cl.map_shared_rank(&f_hi[0][0], (unsigned)rk)[g * 32 + sx] = hi;
+        }
+      }
+    }
+    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
+    if (tid < GT) s_cnt[tid] = 0;
+    cluster_arrive();
+    cluster_wait();             // phase B: all ranges in every CTA
+    if (tid < GT) {
+      const QuantScale qs = quant_scale(f_lo[tid], f_hi[tid], M, p.scale);
+      s_inv[tid] = qs.inv;
+      s_margin[tid] = qs.margin;
+      if (me == 0) p.margin[(int64_t)u * GT + tid] = qs.margin;
+    }
+    __syncthreads();
+    unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
+    {
+      const int qmax = qmax_for(M), j = tid;
+      uint32_t code[GT];
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int sx = s_begin + kk;
+        if (sx < s_end) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) code[g] = quant_code(tv[kk][g], f_lo[g][sx], s_inv[g], qmax);
+          put_entry<CS, GT>(gimg, sx, j, code);
+        }
+      }
+      for (int sx = s_begin + 2; sx < s_end; ++sx) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+          code[g] = quant_code(p.texact[(((int64_t)u * GT + g) * CS + sx) * 256 + j], f_lo[g][sx], s_inv[g], qmax);
+        put_entry<CS, GT>(gimg, sx, j, code);
+      }
+      // padding subspaces [M, CS): zero entries, written by the owner of the
+      // group (rank 0 for groups without a real subspace)
+#pragma unroll
+      for (int g = 0; g < GT; ++g) code[g] = 0u;
+      for (int sx = M; sx < CS; ++sx) {
+        const int grp = sx / GS;
+        const int own = grp < ngm ? ((grp + 1) * R - 1) / ngm : 0;
+        if (own == me) put_entry<CS, GT>(gimg, sx, j, code);
+      }
+    }
+    cluster_arrive();           // phase C: the image is complete in memory
+#pragma unroll
+    for (int it = 0; it < HT; ++it) {
+      const int t = t0 + it * K6_THREADS + tid;
+      if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
+      else {
+#pragma unroll
+        for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
+      }
+    }
+    cluster_wait();
+    for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
+    cp_async_wait_all();
+    __syncthreads();
+  } else {
+    // ---- first half of this thread's codes, loaded before waiting for K5 -----
+#pragma unroll
+    for (int it = 0; it < HT; ++it) {
+      const int t = t0 + it * K6_THREADS + tid;
+      if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
+      else {
+#pragma unroll
+        for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
+      }
+    }
+    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
+    if (tid < GT) s_cnt[tid] = 0;
+    pdl_wait();
+    {
+      const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
+      for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
+    }
+    if (tid < GT) s_margin[tid] = p.margin[(int64_t)u * GT + tid];
+    cp_async_wait_all();
+    __syncthreads();
+  }
+
+  // ---- quantised scores, kept in registers; histogram of all of them --------
   const int r = lane % CS;
   int colidx[CS];
 #pragma unroll
@@ -460,9 +684,6 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     colidx[uu] = Q::rb_of(s) * 256 * Q::COLS + Q::col_of(lane, s);
   }
   uint32_t accs[K6_TPT][Q::NACC];
-  int mxv[GT];
-#pragma unroll
-  for (int g = 0; g < GT; ++g) mxv[g] = -1;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     if (half == 1) {
@@ -499,75 +720,27 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       }
       if (t >= lo_t && t < hi_t) {
 #pragma unroll
-        for (int g = 0; g < GT; ++g) mxv[g] = max(mxv[g], approx_of<GT>(accs[ti], g));
+        for (int g = 0; g < GT; ++g) {
+          const int bin = approx_of<GT>(accs[ti], g) >> HSHIFT;
+          atomicAdd(&hist[g * HWORDS + (bin >> 1)], 1u << (16 * (bin & 1)));
+        }
       }
     }
   }
 
-  // ---- threshold: coarse (per-thread maxima), then refined (all tokens) -----
-  // Coarse histograms hold 256 bins per head, refined ones REFINE_BINS.
-  const int maxv = M * qmax_for(M);
-  int sh = 0;
-  while ((maxv >> sh) > 255) ++sh;
-#pragma unroll
-  for (int g = 0; g < GT; ++g)
-    if (mxv[g] >= 0) atomicAdd(&hist[g * 256 + (mxv[g] >> sh)], 1u);
-  const uint32_t kp = (uint32_t)cr.kp;
-  if constexpr (CL) pool_cluster<GT * 256>(hist, red); else __syncthreads();
+  // ---- threshold: lower edge of the bin holding the k'-th score, less the band
+  if constexpr (FUSED) pool_cluster<GT * HWORDS>(hist, full, R, me); else __syncthreads();
   if (warp < GT) {
     const int g = warp;
-    uint32_t bins[16];
-    int top = -1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) bins[i] = hist[g * 256 + lane * 8 + i];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) if (bins[i]) top = lane * 8 + i;
-    top = __reduce_max_sync(0xffffffffu, top + 1) - 1;
-    int bstar;
-    uint32_t above;
-    scan_top<GT>(bins, 8, kp, lane, bstar, above);
-    int alb = -1, sh2 = 0;
-    if (bstar >= 0) {
-      alb = bstar << sh;
-      const int span = ((top + 1) << sh) - alb;
-      while ((span >> sh2) >= REFINE_BINS) ++sh2;
-    }
-    if (lane == 0) { s_alb[g] = alb; s_sh2[g] = sh2; }
+    const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
+    if (lane == 0)
+      s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
   __syncthreads();
-  for (int i = tid; i < GT * REFINE_BINS; i += K6_THREADS) hist[i] = 0;
-  __syncthreads();
-#pragma unroll
-  for (int ti = 0; ti < K6_TPT; ++ti) {
-    const int t = t0 + ti * K6_THREADS + tid;
-    if (t < lo_t || t >= hi_t) continue;
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      const int a = approx_of<GT>(accs[ti], g), alb = s_alb[g];
-      if (alb >= 0 && a >= alb) atomicAdd(&hist[g * REFINE_BINS + ((a - alb) >> s_sh2[g])], 1u);
-    }
-  }
-  if constexpr (CL) pool_cluster<GT * REFINE_BINS>(hist, red); else __syncthreads();
-  if (warp < GT) {
-    const int g = warp;
-    constexpr int PER = REFINE_BINS / 32;
-    uint32_t bins[16];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) bins[i] = hist[g * REFINE_BINS + lane * PER + i];
-    int bstar;
-    uint32_t above;
-    scan_top<GT>(bins, PER, kp, lane, bstar, above);
-    int thr = -(1 << 30);
-    if (s_alb[g] >= 0 && bstar >= 0) thr = s_alb[g] + (bstar << s_sh2[g]) - s_margin[g];
-    if (lane == 0) s_thr[g] = (s_margin[g] >= (1 << 30)) ? -(1 << 30) : thr;
-  }
-  // the other CTAs of the cluster may still be gathering from `red`
-  if constexpr (CL) cooperative_groups::this_cluster().sync(); else __syncthreads();
 
-  // ---- emit candidates: token index and its code row --------------------------
-  const int64_t cbase_idx = ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
-  uint32_t* cand = p.cand_idx + cbase_idx;
-  uint8_t* ccode = p.cand_code + cbase_idx * CS;
+  // ---- candidates: list (token per (head, slot)), then exact rescoring -------
+  uint32_t* list = hist;   // [GT][CAND_MAX], the histograms are dead
+  static_assert(CAND_MAX <= HWORDS, "candidate list must fit the histogram space");
 #pragma unroll
   for (int ti = 0; ti < K6_TPT; ++ti) {
     const int t = t0 + ti * K6_THREADS + tid;
@@ -583,19 +756,38 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         if (lane == leader) basep = atomicAdd(&s_cnt[g], __popc(m));
         basep = __shfl_sync(0xffffffffu, basep, leader);
         const int slot = basep + __popc(m & ((1u << lane) - 1u));
-        if (pred && slot < CAND_MAX) {
-          cand[g * CAND_MAX + slot] = (uint32_t)t;
-          uint32_t cw[Q::W];
-          load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
-          uint32_t* dst = reinterpret_cast<uint32_t*>(ccode + ((int64_t)g * CAND_MAX + slot) * CS);
-#pragma unroll
-          for (int i = 0; i < Q::W; ++i) dst[i] = cw[i];
-        }
+        if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)t;
       }
     }
   }
   __syncthreads();
-  if (tid < GT) cnt_out[tid] = (tid < p.G && s_cnt[tid] > CAND_MAX) ? -1 : s_cnt[tid];
+  if (tid == 0) {
+    int acc = 0;
+    for (int g = 0; g < GT; ++g) { s_nl[g] = acc; acc += (g < p.G) ? min(s_cnt[g], CAND_MAX) : 0; }
+  }
+  __syncthreads();
+  const int n_items = s_nl[GT - 1] + ((GT - 1 < p.G) ? min(s_cnt[GT - 1], CAND_MAX) : 0);
+  uint64_t* keys = p.cand_key + ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
+  const float scale = p.scale;
+  for (int i = tid; i < n_items; i += K6_THREADS) {
+    int g = 0;
+#pragma unroll
+    for (int k = 1; k < GT; ++k) if (i >= s_nl[k]) g = k;
+    const int slot = i - s_nl[g];
+    if (s_cnt[g] > CAND_MAX) continue;   // overflowed: the chunk is rescanned exactly
+    const uint32_t t = list[g * CAND_MAX + slot];
+    uint32_t cw[Q::W];
+    load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
+    const float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
+    float e[CS];
+#pragma unroll
+    for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + s * 256 + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu)) : 0.f;
+    float sum = 0.f;   // reference order: ((0 + T0[c0]) + T1[c1]) + ...
+#pragma unroll
+    for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
+    keys[g * CAND_MAX + slot] = sel_key(fmul(sum, scale), t);
+  }
+  if (tid < GT) cnt_out[tid] = (tid < p.G && s_cnt[tid] > CAND_MAX) ? -1 : (tid < p.G ? s_cnt[tid] : 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -813,7 +1005,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   int* sel = reinterpret_cast<int*>(hist + 1024);                            // [TOPK_MAX]
   float* part = reinterpret_cast<float*>(sel + TOPK_MAX);                    // [NW][D + 2]
   __shared__ float s_q[D];
-  __shared__ int s_n, s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
+  __shared__ int s_n, s_over, s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
   __shared__ SelShared s_sel;
 
   const int Hq = p.Hkv * p.G;
@@ -853,71 +1045,44 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   } else {
     explicit_sel = true;
     const int M = p.M;
-    // exact sub-table of this head (written by K5)
-    const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
-    for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
     const int64_t cbase_idx = (int64_t)u * p.n_chunks * p.GT;
     for (int c = tid; c < p.n_chunks; c += K7_THREADS) s_cnt[c] = p.cand_cnt[cbase_idx + (int64_t)c * p.GT + g];
-    cp_async_wait_all();
     __syncthreads();
     if (tid == 0) {
-      int acc = 0;
-      for (int c = 0; c < p.n_chunks; ++c) { s_off[c] = acc; acc += s_cnt[c] > 0 ? s_cnt[c] : 0; }
+      int acc = 0, over = 0;
+      for (int c = 0; c < p.n_chunks; ++c) { s_off[c] = acc; acc += s_cnt[c] > 0 ? s_cnt[c] : 0; over |= s_cnt[c] < 0; }
       s_off[p.n_chunks] = acc;
+      s_over = over;
     }
     __syncthreads();
+    if (s_over) {   // exact sub-table of this head, for the rescan of overflowed chunks
+      const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
+      for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
+    }
     const int n_listed = s_off[p.n_chunks];
-    // listed candidates: index + code row written by the candidate stage, up to
-    // RPT per thread loaded together (one memory round trip per pass)
-    constexpr int RPT = 4;
-    for (int base = 0; base < n_listed; base += K7_THREADS * RPT) {
-      if (s_n + K7_THREADS * RPT > K7_CAP) {
+    // listed candidates: selection keys (exact scores) written by the candidate stage
+    for (int base = 0; base < n_listed; base += K7_CAP / 2) {
+      if (s_n + K7_CAP / 2 > K7_CAP) {
         select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
         if (tid == 0) s_n = min(s_n, cr.kp);
         __syncthreads();
       }
-      uint32_t tok[RPT], cw[RPT][8];
-      bool ok[RPT];
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        const int i = base + r * K7_THREADS + tid;
-        ok[r] = i < n_listed;
-        tok[r] = 0;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) cw[r][w] = 0;
-        if (ok[r]) {
-          int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= i < s_off[c + 1]
-          while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_off[mid] <= i) lo = mid; else hi = mid - 1;
-          }
-          const int64_t e = (cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (i - s_off[lo]);
-          tok[r] = p.cand_idx[e];
-          const uint8_t* row = p.cand_code + e * p.CS;
-          if (p.CS == 16) {
-            const uint4 v = *reinterpret_cast<const uint4*>(row);
-            cw[r][0] = v.x; cw[r][1] = v.y; cw[r][2] = v.z; cw[r][3] = v.w;
-          } else if (p.CS == 8) {
-            const uint2 v = *reinterpret_cast<const uint2*>(row);
-            cw[r][0] = v.x; cw[r][1] = v.y;
-          } else if (p.CS == 4) {
-            cw[r][0] = *reinterpret_cast<const uint32_t*>(row);
-          } else {
-            const uint4 v = *reinterpret_cast<const uint4*>(row), v2 = *reinterpret_cast<const uint4*>(row + 16);
-            cw[r][0] = v.x; cw[r][1] = v.y; cw[r][2] = v.z; cw[r][3] = v.w;
-            cw[r][4] = v2.x; cw[r][5] = v2.y; cw[r][6] = v2.z; cw[r][7] = v2.w;
-          }
+      const int nb = min(K7_CAP / 2, n_listed - base);
+      for (int i = tid; i < nb; i += K7_THREADS) {
+        const int li = base + i;
+        int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
         }
-      }
-#pragma unroll
-      for (int r = 0; r < RPT; ++r) {
-        if (!ok[r]) continue;
-        float sum = 0.f;
-        for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + ((cw[r][s >> 2] >> (8 * (s & 3))) & 0xffu)]);
-        keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), tok[r]);
+        keys[s_n + i] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
       }
       __syncthreads();
+      if (tid == 0) s_n += nb;
+      __syncthreads();
     }
+    cp_async_wait_all();
+    __syncthreads();
     // overflowed chunks: rescan every non-sink token of the chunk
     const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
     for (int c = 0; c < p.n_chunks; ++c) {

@@ -61,26 +61,30 @@ static int ensure_smem(K kernel, size_t bytes) {
   return HOKV_OK;
 }
 
-// Programmatic (PDL) launch; cluster_x > 0 also groups cluster_x consecutive
+// Extended launch: `pdl` allows a programmatic (early) start behind the
+// previous kernel of the stream; cluster_x > 0 groups cluster_x consecutive
 // blocks along x into one thread-block cluster.
 template <typename K>
-static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st, const Cdc03P& p, const char* what,
-                      int cluster_x = 0) {
+static int launch_ex(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st, const Cdc03P& p, const char* what,
+                     bool pdl, int cluster_x = 0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = sm;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  int na = 1;
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   if (cluster_x > 0) {
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = (unsigned)cluster_x;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    na = 2;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
@@ -94,25 +98,28 @@ static int launch_pdl(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t s
 
 // Stage 1: K5 (tables, ordinary launch: it reads the queries) then K6
 // (candidates, programmatic launch: it prefetches its codes while K5 runs).
+// Stage 1.  Up to K6_CLUSTER_MAX chunks per unit: one clustered kernel that
+// builds the tables and streams the candidates (ordinary launch: it reads the
+// queries).  Longer contexts: K5 (tables) then K6 (programmatic launch that
+// loads its codes while K5 runs).
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
+  const size_t sm6 = Q::BYTES + (size_t)GT * HWORDS * 4;
+  const dim3 grid6((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
+  if (p.n_chunks <= K6_CLUSTER_MAX) {
+    const size_t smc = sm6 + (size_t)GT * HWORDS * 4;   // pooled histograms
+    if (int e = ensure_smem(k6_candidates<CS, GT, true>, smc)) return e;
+    return launch_ex(k6_candidates<CS, GT, true>, grid6, dim3(K6_THREADS), smc, st, p, "k6_candidates (fused)",
+                     false, p.n_chunks);
+  }
   const size_t sm5 = (size_t)p.M * stage_rows(p.slots, p.M * p.sd) * p.sd * 4;
   if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
   k5_tables<CS, GT><<<dim3((unsigned)(p.B * p.Hkv), (unsigned)GT), K5_THREADS, sm5, st>>>(p);
   if (int e = check_launch("k5_tables")) return e;
-  const size_t sm6 = Q::BYTES + (size_t)GT * REFINE_BINS * 4;
-  const dim3 grid6((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
-  if (p.n_chunks >= 2 && p.n_chunks <= K6_CLUSTER_MAX) {
-    // one cluster per (sequence, KV head): a unit-wide threshold
-    const size_t smc = sm6 + (size_t)GT * REFINE_BINS * 2;
-    if (int e = ensure_smem(k6_candidates<CS, GT, true>, smc)) return e;
-    return launch_pdl(k6_candidates<CS, GT, true>, grid6, dim3(K6_THREADS), smc, st, p, "k6_candidates",
-                      p.n_chunks);
-  }
   if (int e = ensure_smem(k6_candidates<CS, GT, false>, sm6)) return e;
-  return launch_pdl(k6_candidates<CS, GT, false>, grid6, dim3(K6_THREADS), sm6, st, p, "k6_candidates");
+  return launch_ex(k6_candidates<CS, GT, false>, grid6, dim3(K6_THREADS), sm6, st, p, "k6_candidates", true);
 }
 
 static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
@@ -138,8 +145,8 @@ static int launch_k7(const Cdc03P& p, cudaStream_t st) {
   const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 +
                     (size_t)(K7_THREADS / 32) * (D + 2) * 4;
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
-  return launch_pdl(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
-                    "k7_select_attend");
+  return launch_ex(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
+                   "k7_select_attend", true);
 }
 
 template <typename KVT>
@@ -425,9 +432,9 @@ static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct Plan {
   int n_chunks, chunk, GT, qimg_bytes;
-  size_t cand_idx_bytes, cand_cnt_bytes, cand_code_bytes, qimg_total, texact_bytes, margin_bytes;
+  size_t cand_key_bytes, cand_cnt_bytes, qimg_total, texact_bytes, margin_bytes;
   size_t total() const {
-    return cand_idx_bytes + cand_cnt_bytes + cand_code_bytes + qimg_total + texact_bytes + margin_bytes;
+    return cand_key_bytes + cand_cnt_bytes + qimg_total + texact_bytes + margin_bytes;
   }
 };
 
@@ -477,9 +484,8 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
     return fail(HOKV_ERR_UNSUPPORTED, "cdc03: capacity %lld needs %d chunks > %d", (long long)a->capacity,
                 pl->n_chunks, MAX_CHUNKS);
   const size_t slots = (size_t)units * pl->n_chunks * pl->GT * CAND_MAX;
-  pl->cand_idx_bytes = a256(slots * 4);
+  pl->cand_key_bytes = a256(slots * 8);
   pl->cand_cnt_bytes = a256((size_t)units * pl->n_chunks * pl->GT * 4);
-  pl->cand_code_bytes = a256(slots * a->code_bytes);
   pl->qimg_bytes = qimg_bytes_for(a->code_bytes, pl->GT);
   pl->qimg_total = a256((size_t)units * pl->qimg_bytes);
   pl->texact_bytes = a256((size_t)units * pl->GT * a->code_bytes * 256 * 4);
@@ -508,11 +514,9 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   p.seq_len = a->seq_len;
   p.sel_idx = a->sel_idx; p.sel_score = a->sel_score; p.sel_count = a->sel_count;
   unsigned char* w = static_cast<unsigned char*>(a->workspace);
-  p.cand_idx = reinterpret_cast<uint32_t*>(w);
-  p.cand_cnt = reinterpret_cast<int*>(w + pl.cand_idx_bytes);
-  w += pl.cand_idx_bytes + pl.cand_cnt_bytes;
-  p.cand_code = w;
-  w += pl.cand_code_bytes;
+  p.cand_key = reinterpret_cast<uint64_t*>(w);
+  p.cand_cnt = reinterpret_cast<int*>(w + pl.cand_key_bytes);
+  w += pl.cand_key_bytes + pl.cand_cnt_bytes;
   p.qimg = w;
   w += pl.qimg_total;
   p.texact = reinterpret_cast<float*>(w);

@@ -178,6 +178,20 @@ def test_store_long_context_16k():
     assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "16k") <= 4
 
 
+def test_store_long_context_20k_chunk_thresholds():
+    """20K tokens: 10 candidate chunks per unit, more than one cluster holds,
+    so the tables come from their own kernel and each chunk ranks alone."""
+    st, q, lens = _store(1, 1, 4, 128, 20000, 16, torch.bfloat16, seed=11)
+    assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "20k") <= 4
+
+
+def test_store_group_of_three_uneven_cluster():
+    """G = 3 query heads per KV head (one padded score lane) and 3 chunks per
+    unit, so the cluster splits 4 subspace groups unevenly over 3 CTAs."""
+    st, q, lens = _store(2, 2, 3, 64, 5000, 8, torch.float16, seed=13, seq_lens=[5000, 4100])
+    assert _check_store(st, q, lens, 0.125, 128, 4, 256, "g3") <= 4
+
+
 @pytest.mark.parametrize("S,top_k,sink,hot", [
     (100, 128, 4, 256),    # shorter than the hot window: no cold tokens
     (300, 128, 4, 256),    # cold range shorter than top_k: all cold selected
@@ -194,8 +208,8 @@ def test_store_edge_cases(S, top_k, sink, hot):
 
 def test_ties_and_candidate_overflow():
     """Keys drawn from 8 distinct rows: exact score ties everywhere.  The lower
-    token index wins, and with 80 (sequence, head) units the chunks hold 2048
-    tokens, so candidate lists overflow and those chunks are rescanned exactly."""
+    token index wins; the tied band around the k'-th score overflows the
+    candidate lists, and those chunks are rescanned exactly."""
     from helix_online_kv.cdc03 import CDC03Store
     B, H, S, D, M = 2, 40, 6000, 64, 8
     st = CDC03Store(B, 1, H, D, S, n_subspaces=M, dtype=torch.float16)
