@@ -557,6 +557,54 @@ int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream) {
   return dispatch_k7(p, a->kv_dtype, S(stream));
 }
 
+// ---------------------------------------------------------------------------
+// hokv_cdc03_decode with library-owned scratch: for callers that cannot
+// allocate device memory (see hokv.h).  The array lives in this file; host
+// code only ever uses the device address cudaGetSymbolAddress returns for it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_cdc03_scratch[HOKV_CDC03_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_cdc03_scratch on the current device, looked up once per
+// device (with that device current) and kept.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static std::map<int, void*> addr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "cdc03_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  std::lock_guard<std::mutex> g(mu);
+  auto it = addr.find(dev);
+  if (it == addr.end()) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_cdc03_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      (void)cudaGetLastError();
+      return fail(HOKV_ERR_CUDA, "cdc03_decode_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    }
+    it = addr.emplace(dev, ptr).first;
+  }
+  *out = it->second;
+  return HOKV_OK;
+}
+
+int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream) {
+  HOKV_REQUIRE(a, "cdc03_decode_noalloc: null args");
+  size_t need = 0;
+  if (int st = hokv_cdc03_workspace_size(a, &need)) return st;
+  if (need > HOKV_CDC03_NOALLOC_SCRATCH_BYTES)
+    return fail(HOKV_ERR_WORKSPACE,
+                "cdc03_decode_noalloc: this configuration needs %zu bytes of scratch, more than the %zu bytes the "
+                "library holds; use hokv_cdc03_decode with a caller-provided workspace",
+                need, (size_t)HOKV_CDC03_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  hokv_cdc03_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = HOKV_CDC03_NOALLOC_SCRATCH_BYTES;
+  return hokv_cdc03_decode(&b, stream);
+}
+
 int hokv_dense_attention(const float* q, const float* K, const float* V, int head_dim, int64_t seq_len, int mul_f64,
                          double scale, int store_flags, const uint8_t* mask, void* scores, void* out, void* workspace,
                          size_t workspace_bytes, void* stream) {

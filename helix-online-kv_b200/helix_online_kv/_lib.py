@@ -95,6 +95,7 @@ _SIGS = {
     "hokv_cdc03_decode": (_c_int, [ctypes.POINTER(Cdc03Args), _vp]),
     "hokv_cdc03_candidates": (_c_int, [ctypes.POINTER(Cdc03Args), _vp]),
     "hokv_cdc03_attend": (_c_int, [ctypes.POINTER(Cdc03Args), _vp]),
+    "hokv_cdc03_decode_noalloc": (_c_int, [ctypes.POINTER(Cdc03Args), _vp]),
     "hokv_age_tokens": (_c_int, [ctypes.POINTER(Cdc03Args), _vp, _vp, _c_int, _vp]),
     "hokv_dense_attention": (_c_int, [_vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f64, _c_int, _vp, _vp, _vp, _vp,
                                       _c_sz, _vp]),

@@ -245,6 +245,33 @@ int hokv_cdc03_candidates(const hokv_cdc03_args* a, void* stream);
  * cold tokens plus the hot window.  Reads the workspace stage 1 wrote. */
 int hokv_cdc03_attend(const hokv_cdc03_args* a, void* stream);
 
+/* hokv_cdc03_decode for callers that cannot allocate device memory.  No
+ * counterpart in the reference (its NumPy path allocates as it goes).
+ *
+ * Who needs it: a plugin loaded by a serving runtime that reserves nearly all
+ * HBM for its own KV pool at start-up and hands its plugins no allocator.
+ * There cudaMalloc either fails for lack of memory or, since it synchronises
+ * with the device, stalls a decode step that must not block; the caller also
+ * has no spare buffer to pass as `workspace`.
+ *
+ * What it does: the same two stages as hokv_cdc03_decode, with the scratch
+ * taken from one array of HOKV_CDC03_NOALLOC_SCRATCH_BYTES that the library
+ * itself holds on every device it is loaded on, until the process exits.
+ * a->workspace and a->workspace_bytes are ignored; inputs and outputs stay
+ * the caller's.  A configuration whose hokv_cdc03_workspace_size exceeds the
+ * limit is rejected with HOKV_ERR_WORKSPACE before anything is launched
+ * (16 MiB covers 8 sequences x 8 KV heads x 4 query heads at 16K tokens with
+ * 16 subspaces).  The library allocates nothing on this path.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current) and keeps it; make that first call before any stream
+ * capture.  All calls on a device share the array and nothing in it has to
+ * start at zero: each call writes every scratch byte it later reads, so the
+ * previous call's contents are harmless.  Calls that overlap on the GPU
+ * (other streams, other host threads) race on the array: order them. */
+#define HOKV_CDC03_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream);
+
 /* ------------------------------------------------------------------------
  * Tier aging (AgingPolicy.tier_boundary, aging_policy.py:42-56, applied in
  * place): for every (b, h) assign the PQ code of each token in
