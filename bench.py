@@ -404,7 +404,7 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": q.numel() * q.element_size(),
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
         "vq_assign": {"value": as_gbs, "unit": "GB/s", "frac": as_gbs / peak, "vectors": units * n_new,
-                      "ms": as_ms, "kernel": "k_pq_assign (fp32 CUDA cores)"},
+                      "ms": as_ms, "kernel": "k_pq_assign_seq (fp32 CUDA cores, 4 vectors per thread in registers)"},
         "gpu_launches": args.steps * Ls * (2 if fused else 3),
         "clocks": clk.summary(),
         "setup_s": t_setup,

@@ -741,22 +741,36 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   // ---- candidates: list (token per (head, slot)), then exact rescoring -------
   uint32_t* list = hist;   // [GT][CAND_MAX], the histograms are dead
   static_assert(CAND_MAX <= HWORDS, "candidate list must fit the histogram space");
+  {   // per-warp counts first, one atomic per (warp, head), then the slots
+    int wc[GT];
 #pragma unroll
-  for (int ti = 0; ti < K6_TPT; ++ti) {
-    const int t = t0 + ti * K6_THREADS + tid;
-    const bool valid = t >= lo_t && t < hi_t;
+    for (int g = 0; g < GT; ++g) wc[g] = 0;
 #pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      if (g >= p.G) break;   // uniform across the block
-      const bool pred = valid && approx_of<GT>(accs[ti], g) >= s_thr[g];
-      const unsigned m = __ballot_sync(0xffffffffu, pred);
-      if (m) {
-        const int leader = __ffs(m) - 1;
-        int basep = 0;
-        if (lane == leader) basep = atomicAdd(&s_cnt[g], __popc(m));
-        basep = __shfl_sync(0xffffffffu, basep, leader);
-        const int slot = basep + __popc(m & ((1u << lane) - 1u));
+    for (int ti = 0; ti < K6_TPT; ++ti) {
+      const int t = t0 + ti * K6_THREADS + tid;
+      const bool valid = t >= lo_t && t < hi_t;
+#pragma unroll
+      for (int g = 0; g < GT; ++g)
+        wc[g] += __popc(__ballot_sync(0xffffffffu, valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g]));
+    }
+    int mine = 0;
+#pragma unroll
+    for (int g = 0; g < GT; ++g) if (lane == g) mine = wc[g];
+    int basev = 0;
+    if (lane < p.G && mine > 0) basev = atomicAdd(&s_cnt[lane], mine);
+#pragma unroll
+    for (int g = 0; g < GT; ++g) wc[g] = __shfl_sync(0xffffffffu, basev, g);   // running slot per head
+#pragma unroll
+    for (int ti = 0; ti < K6_TPT; ++ti) {
+      const int t = t0 + ti * K6_THREADS + tid;
+      const bool valid = t >= lo_t && t < hi_t;
+#pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        const bool pred = valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g];
+        const unsigned m = __ballot_sync(0xffffffffu, pred);
+        const int slot = wc[g] + __popc(m & ((1u << lane) - 1u));
         if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)t;
+        wc[g] += __popc(m);
       }
     }
   }

@@ -316,6 +316,62 @@ __global__ void __launch_bounds__(256) k_pq_assign(const void* __restrict__ x, i
   }
 }
 
+// Batched assignment in the sequential-FMA order (BLAS sgemm with >= 5 rows,
+// the order every prefill-sized batch gets), SD in {4, 8}: grid
+// (ceil(n / (256 V)), M, n_sets), 256 threads, V vectors per thread held in
+// registers against every centroid of the subspace, read from shared memory
+// as broadcasts (SD * V <= 32 keeps the vectors in registers).  Same
+// arithmetic and tie rule (lowest index) as k_pq_assign.
+template <int SD, int V>
+__global__ void __launch_bounds__(256) k_pq_assign_seq(const void* __restrict__ x, int dtype, int64_t n, int64_t xrs,
+                                                       int64_t xss, const float* __restrict__ cents, int slots,
+                                                       int64_t css, const int* __restrict__ kk, int64_t kss,
+                                                       uint8_t* __restrict__ out, int64_t ors, int64_t oss) {
+  __shared__ float cs[256 * SD];
+  __shared__ float c2[256];
+  const int s = blockIdx.y, set = blockIdx.z;
+  const int tid = threadIdx.x;
+  int k = kk[(int64_t)set * kss + s];
+  k = k < 1 ? 1 : (k > slots ? slots : k);
+  const float* cg = cents + (int64_t)set * css + (int64_t)s * slots * SD;
+  for (int i = tid; i < k * SD; i += blockDim.x) cs[i] = cg[i];
+  __syncthreads();
+  for (int j = tid; j < k; j += blockDim.x) c2[j] = sum_sq(cs + j * SD, SD);
+  float xv[V][SD], x2[V], best[V];
+  int bj[V];
+  const int64_t i0 = (int64_t)blockIdx.x * 256 * V + tid;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int64_t i = i0 + (int64_t)v * 256;
+    const int64_t base = (int64_t)set * xss + (i < n ? i : 0) * xrs + (int64_t)s * SD;
+#pragma unroll
+    for (int d = 0; d < SD; ++d) xv[v][d] = load_as_f32(x, dtype, base + d);
+    x2[v] = sum_sq(xv[v], SD);
+    best[v] = INFINITY;
+    bj[v] = 0x7fffffff;
+  }
+  __syncthreads();
+  for (int j = 0; j < k; ++j) {
+    float c[SD];
+#pragma unroll
+    for (int d = 0; d < SD; ++d) c[d] = cs[j * SD + d];
+    const float cj2 = c2[j];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < SD; ++d) acc = ffma(xv[v][d], c[d], acc);
+      const float dd = l2_expansion(x2[v], acc, cj2);
+      if (dd < best[v] || bj[v] == 0x7fffffff) { best[v] = dd; bj[v] = j; }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int64_t i = i0 + (int64_t)v * 256;
+    if (i < n) out[(int64_t)set * oss + i * ors + s] = (uint8_t)bj[v];
+  }
+}
+
 __global__ void k_pq_decode(const uint8_t* __restrict__ codes, int64_t n, int64_t crs, int M, int sd,
                             const float* __restrict__ cents, int slots, float* __restrict__ out) {
   const int64_t total = n * M * sd;

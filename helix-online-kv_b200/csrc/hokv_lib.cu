@@ -330,6 +330,20 @@ int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, 
   HOKV_REQUIRE(x_dtype == HOKV_F32 || x_dtype == HOKV_F16 || x_dtype == HOKV_BF16, "pq_assign: dtype %d", x_dtype);
   HOKV_REQUIRE(sub_dim <= 1024, "pq_assign: sub_dim %d > 1024", sub_dim);
   if (n == 0) return HOKV_OK;
+  if (dot_order == DOT_SEQ_FMA && (sub_dim == 4 || sub_dim == 8)) {
+    // prefill-sized batches: register-tiled kernel, same arithmetic
+    HOKV_REQUIRE(cdiv(n, 1024) < (1ll << 31) && M <= 65535 && n_sets <= 65535, "pq_assign: grid too large");
+    const dim3 grid((unsigned)cdiv(n, 1024), (unsigned)M, (unsigned)n_sets);
+#define HOKV_PQA(sd_, v_)                                                                                          \
+  if (sub_dim == sd_) {                                                                                          \
+    k_pq_assign_seq<sd_, v_><<<grid, 256, 0, S(stream)>>>(x, x_dtype, n, x_row_stride, x_set_stride, cents,       \
+                                                        cb_slots, cent_set_stride, k, k_set_stride, out,          \
+                                                        out_row_stride, out_set_stride);                          \
+    return check_launch("k_pq_assign_seq");                                                                      \
+  }
+    HOKV_PQA(4, 4) HOKV_PQA(8, 4)
+#undef HOKV_PQA
+  }
   size_t sm = (256 + 8 * (size_t)sub_dim) * 4;
   const size_t cb_sm = (size_t)cb_slots * (sub_dim + 1) * 4;
   int use_smem = (sm + cb_sm) <= 160 * 1024;
