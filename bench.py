@@ -215,6 +215,7 @@ def run_ours(args):
 
     from helix_online_kv import _lib as L
     from helix_online_kv.cdc03 import CDC03Store
+    from helix_online_kv.sharding import max_over_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -283,11 +284,7 @@ def run_ours(args):
             graph.replay()
         ev1.record()
         torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ev0.elapsed_time(ev1), device="cuda")
     barrier()
     ms_step = ms / args.steps
     tokens = B * world * args.steps
@@ -349,11 +346,7 @@ def run_ours(args):
         out_host.copy_(out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), device="cuda")
     e2e_value = tokens / (e2e_ms / 1e3)
 
     # VQ-assign throughput: PQ codes for a fresh 32768-token block of every (b, h) of one layer

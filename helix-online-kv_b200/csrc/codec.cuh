@@ -372,6 +372,62 @@ __global__ void __launch_bounds__(256) k_pq_assign_seq(const void* __restrict__ 
   }
 }
 
+__device__ __forceinline__ float kv_to_f32(float v) { return v; }
+__device__ __forceinline__ float kv_to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float kv_to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Tier aging: PQ codes of the tokens [cold_from[b], cold_to[b]) of every
+// (sequence b, KV head h) from the exact key store, written in place into the
+// code store.  grid (gx, H_kv, B), 256 threads, one warp per (token,
+// subspace) item; the arithmetic and tie rule are those of k_pq_assign.
+template <typename KVT>
+__global__ void __launch_bounds__(256) k_age_tokens(const KVT* __restrict__ k, int64_t kv_sb, int64_t kv_sh, int D,
+                                                    int M, int sd, const float* __restrict__ cb, int64_t cb_sb,
+                                                    int64_t cb_sh, int slots, const int* __restrict__ cbk,
+                                                    int64_t cbk_sb, int64_t cbk_sh, uint8_t* __restrict__ codes,
+                                                    int64_t c_sb, int64_t c_sh, int CS, const int* __restrict__ from,
+                                                    const int* __restrict__ to, int64_t cap, int order) {
+  __shared__ float xs[8][32];
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int t0 = from[b], t1 = to[b];
+  if (t0 < 0 || t1 > cap || t0 > t1) {
+    dev_flag(HOKV_ERR_DEVICE_INPUT);
+    return;
+  }
+  const int64_t n_items = (int64_t)(t1 - t0) * M;
+  const KVT* kb = k + (int64_t)b * kv_sb + (int64_t)h * kv_sh;
+  const float* cbase = cb + (int64_t)b * cb_sb + (int64_t)h * cb_sh;
+  const int* kcount = cbk + (int64_t)b * cbk_sb + (int64_t)h * cbk_sh;
+  uint8_t* cout = codes + (int64_t)b * c_sb + (int64_t)h * c_sh;
+  float* xw = xs[warp];
+  for (int64_t it = (int64_t)blockIdx.x * 8 + warp; it < n_items; it += (int64_t)gridDim.x * 8) {
+    const int64_t t = t0 + it / M;
+    const int s = (int)(it - (it / M) * M);
+    int kk = kcount[s];
+    kk = kk < 1 ? 1 : (kk > slots ? slots : kk);
+    if (lane < sd) xw[lane] = kv_to_f32(kb[t * D + (int64_t)s * sd + lane]);
+    __syncwarp();
+    const float x2 = sum_sq(xw, sd);
+    const float* cs = cbase + (int64_t)s * slots * sd;
+    float best = INFINITY;
+    int bj = 0x7fffffff;
+    for (int j = lane; j < kk; j += 32) {
+      const float* crow = cs + (int64_t)j * sd;
+      const float dd = l2_expansion(x2, dot_order(order, xw, crow, sd), sum_sq(crow, sd));
+      if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, o);
+      if (ob < best || (ob == best && oj < bj)) { best = ob; bj = oj; }
+    }
+    if (lane == 0) cout[t * CS + s] = (uint8_t)(bj == 0x7fffffff ? 0 : bj);
+    __syncwarp();
+  }
+}
+
 __global__ void k_pq_decode(const uint8_t* __restrict__ codes, int64_t n, int64_t crs, int M, int sd,
                             const float* __restrict__ cents, int slots, float* __restrict__ out) {
   const int64_t total = n * M * sd;

@@ -657,8 +657,32 @@ int hokv_scale_f32_to_f64(const float* in, int64_t n, double scale, double* out,
 }
 
 int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* cold_to, int dot_order, void* stream) {
-  (void)a; (void)cold_from; (void)cold_to; (void)dot_order; (void)stream;
-  return fail(HOKV_ERR_UNSUPPORTED, "age_tokens: not built yet");
+  HOKV_REQUIRE(a && cold_from && cold_to, "age_tokens: null argument");
+  HOKV_REQUIRE(a->batch >= 1 && a->kv_heads >= 1 && a->batch <= 65535 && a->kv_heads <= 65535,
+               "age_tokens: batch=%d kv_heads=%d", a->batch, a->kv_heads);
+  HOKV_REQUIRE(a->n_subspaces >= 1 && a->n_subspaces <= a->code_bytes && a->code_bytes <= 32,
+               "age_tokens: M=%d code_bytes=%d", a->n_subspaces, a->code_bytes);
+  const int sd = a->sub_dim > 0 ? a->sub_dim : a->head_dim / a->n_subspaces;
+  HOKV_REQUIRE(sd >= 1 && sd <= 32 && a->n_subspaces * sd <= a->head_dim, "age_tokens: sub_dim %d", sd);
+  HOKV_REQUIRE(a->cb_slots >= 1 && a->cb_slots <= 256, "age_tokens: cb_slots=%d", a->cb_slots);
+  HOKV_REQUIRE(dot_order >= 0 && dot_order <= 2, "age_tokens: dot_order=%d", dot_order);
+  HOKV_REQUIRE(a->k && a->codes && a->codebook && a->cb_k, "age_tokens: null store pointer");
+  HOKV_REQUIRE(a->capacity >= 1, "age_tokens: capacity=%lld", (long long)a->capacity);
+  const int64_t items = a->capacity * a->n_subspaces;
+  const unsigned gx = (unsigned)std::min<int64_t>(64, std::max<int64_t>(1, cdiv(items, 8 * 32)));
+  const dim3 grid(gx, (unsigned)a->kv_heads, (unsigned)a->batch);
+#define HOKV_AGE(T)                                                                                                 \
+  k_age_tokens<T><<<grid, 256, 0, S(stream)>>>(reinterpret_cast<const T*>(a->k), a->kv_stride_b, a->kv_stride_h,   \
+                                               a->head_dim, a->n_subspaces, sd, a->codebook, a->cb_stride_b,       \
+                                               a->cb_stride_h, a->cb_slots, a->cb_k, a->cbk_stride_b,              \
+                                               a->cbk_stride_h, const_cast<uint8_t*>(a->codes), a->code_stride_b, a->code_stride_h, \
+                                               a->code_bytes, cold_from, cold_to, a->capacity, dot_order)
+  if (a->kv_dtype == HOKV_BF16) HOKV_AGE(__nv_bfloat16);
+  else if (a->kv_dtype == HOKV_F16) HOKV_AGE(__half);
+  else if (a->kv_dtype == HOKV_F32) HOKV_AGE(float);
+  else return fail(HOKV_ERR_INVALID, "age_tokens: kv dtype %d", a->kv_dtype);
+#undef HOKV_AGE
+  return check_launch("k_age_tokens");
 }
 
 }  // extern "C"

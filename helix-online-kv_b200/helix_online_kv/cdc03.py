@@ -90,6 +90,54 @@ class CDC03Store:
                                            L.ptr(self.cb_k[layer, b]), self.M, L.ptr(out), self.CS,
                                            self.cap * self.CS, self.H, order, L.stream()), "pq_assign")
 
+    # ---- tier aging ----------------------------------------------------------
+    def _store_args(self, layer: int) -> L.Cdc03Args:
+        a = L.Cdc03Args()
+        a.batch, a.kv_heads, a.q_per_kv, a.head_dim = self.B, self.H, 1, self.D
+        a.n_subspaces, a.sub_dim, a.code_bytes, a.cb_slots = self.M, self.sd, self.CS, SLOTS
+        kl = self.k[layer]
+        a.k, a.v, a.kv_dtype = kl.data_ptr(), self.v[layer].data_ptr(), L.dtype_code(kl)
+        a.kv_stride_b, a.kv_stride_h = kl.stride(0), kl.stride(1)
+        a.capacity = self.cap
+        cl = self.codes[layer]
+        a.codes, a.code_stride_b, a.code_stride_h = cl.data_ptr(), cl.stride(0), cl.stride(1)
+        cb, ck = self.codebook[layer], self.cb_k[layer]
+        a.codebook, a.cb_stride_b, a.cb_stride_h = cb.data_ptr(), cb.stride(0), cb.stride(1)
+        a.cb_k, a.cbk_stride_b, a.cbk_stride_h = ck.data_ptr(), ck.stride(0), ck.stride(1)
+        a.seq_len = self.seq_len.data_ptr()
+        return a
+
+    def age(self, layer: int, cold_from, cold_to, order: int | None = None):
+        """PQ codes, in place, for tokens [cold_from[b], cold_to[b]) of every
+        sequence b (device int32 tensors [B]); the tokens leaving the hot window
+        (AgingPolicy.tier_boundary, aging_policy.py:42-56)."""
+        cf = cold_from.to(device=self.k.device, dtype=torch.int32).contiguous()
+        ct = cold_to.to(device=self.k.device, dtype=torch.int32).contiguous()
+        if order is None:
+            order = L.dot_order_for(1, self.sd)
+        a = self._store_args(layer)
+        L.check(L.lib().hokv_age_tokens(ctypes.byref(a), L.ptr(cf), L.ptr(ct), order, L.stream()), "age_tokens")
+
+    def append(self, k_new, v_new, hot_window: int = 256, order: int | None = None):
+        """One decode step's new token for every layer and sequence:
+        k_new/v_new [L, B, H_kv, D] go to position seq_len[b]; the token that
+        leaves the hot window (position seq_len[b] - hot_window) gets its PQ
+        codes; seq_len grows by one.  Device-side only (no host sync)."""
+        if k_new.shape != (self.L, self.B, self.H, self.D) or v_new.shape != k_new.shape:
+            raise ValueError(f"Expected shape {(self.L, self.B, self.H, self.D)}, got {tuple(k_new.shape)}")
+        # a full sequence keeps its rows; its length still grows, so the next
+        # decode reports HOKV_ERR_DEVICE_INPUT through the device status
+        full = (self.seq_len >= self.cap)[:, None, None, None]
+        pos = torch.clamp(self.seq_len.long(), max=self.cap - 1)
+        ar = torch.arange(self.B, device=pos.device)
+        for store, new in ((self.k, k_new), (self.v, v_new)):
+            store[:, ar, :, pos] = torch.where(full, store[:, ar, :, pos], new.to(store.dtype).permute(1, 0, 2, 3))
+        cold_from = torch.clamp(self.seq_len - hot_window, min=0)
+        cold_to = torch.clamp(self.seq_len + 1 - hot_window, min=0)
+        for layer in range(self.L):
+            self.age(layer, cold_from, cold_to, order)
+        self.seq_len += 1
+
     # ---- decode ---------------------------------------------------------------
     def args(self, layer: int, q, out, scale: float, top_k: int = 128, sink_tokens: int = 4,
              hot_window: int = 256, sel_idx=None, sel_score=None, sel_count=None) -> L.Cdc03Args:

@@ -278,6 +278,12 @@ int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream);
  * [cold_from[b], cold_to[b]) from the exact store and write it into the
  * code store.  The reference computes the boundary but never moves tokens
  * (compressed_cache.py:51); this is the device-side demotion step.
+ * Uses the store fields of `a` (k, kv_dtype, strides, capacity, codes,
+ * codebook, cb_k, n_subspaces, sub_dim, code_bytes, cb_slots); cold_from and
+ * cold_to are device int32 [batch].  dot_order as for hokv_pq_assign
+ * (hokv_dot_order_for(1, sub_dim) reproduces a one-token assign, the decode
+ * step's case).  A range outside [0, capacity] sets HOKV_ERR_DEVICE_INPUT
+ * in the device status and leaves that sequence's codes untouched.
  * ---------------------------------------------------------------------- */
 int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* cold_to,
                     int dot_order, void* stream);

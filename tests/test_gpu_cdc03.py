@@ -121,7 +121,7 @@ def _store(B, Hkv, G, D, S, M, dtype, seed=0, seq_lens=None, hot=256, cal=128):
     return st, torch.from_numpy(Q).to(dtype).cuda(), lens
 
 
-def _check_store(st, q, lens, scale, top_k, sink, hot, label):
+def _check_store(st, q, lens, scale, top_k, sink, hot, label, exclude_rows=None):
     out, (sel, ssc, cnt) = st.decode(0, q, scale, top_k, sink, hot, out_dtype=torch.float32, return_selection=True)
     torch.cuda.synchronize()
     from helix_online_kv import _lib
@@ -138,7 +138,11 @@ def _check_store(st, q, lens, scale, top_k, sink, hot, label):
             cbk = st.codebook[0, b, h].cpu().numpy()
             cents = [cbk[s, :kk[s]] for s in range(st.M)]
             codes = st.codes[0, b, h, :S, :st.M].cpu().numpy()
-            np.testing.assert_array_equal(codes, O.pq_assign(Kh, cents), err_msg=f"{label} codes b{b} h{h}")
+            # the codes the decode reads: the cold range (rows aged one at a
+            # time are checked against a one-token assign by their own test)
+            Sc = max(0, S - hot)
+            rows = [t for t in range(Sc) if t not in (exclude_rows or {}).get(b, ())]
+            np.testing.assert_array_equal(codes[rows], O.pq_assign(Kh, cents)[rows], err_msg=f"{label} codes b{b} h{h}")
             for g in range(G):
                 hq = h * G + g
                 qv = q[b, hq].float().cpu().numpy()
@@ -243,3 +247,68 @@ def test_hot_window_zero_equals_hybrid(golden):
         got = sel[0, hq, :int(cnt[0, hq])].cpu().numpy()
         _assert_selection(got, golden[f"c0m8_q{hq}_approx"], 128, 4, f"hq{hq}")
         np.testing.assert_allclose(out[0, hq].cpu().numpy(), golden[f"c0m8_q{hq}_out"], atol=2e-3)
+
+
+def test_age_tokens_and_append():
+    """Tier aging in place: tokens leaving the hot window get the PQ codes a
+    one-token assign gives (GEMV order), ragged per sequence; append() writes
+    the new rows, ages the boundary token and grows the lengths; a decode after
+    it matches the oracle at the new length."""
+    from helix_online_kv.cdc03 import CDC03Store
+    from helix_online_kv import _lib
+    B, H, G, D, S, M, hot = 2, 2, 4, 64, 1600, 8, 256
+    lens = [1500, 1200]
+    K, V = O.gen_kv(31, B, H, S, D)
+    st = CDC03Store(B, 2, H, D, S, n_subspaces=M, dtype=torch.float16)
+    for layer in range(2):
+        st.k[layer, :, :, :S] = torch.from_numpy(K).half().cuda()
+        st.v[layer, :, :, :S] = torch.from_numpy(V).half().cuda()
+        st.calibrate(layer, 128)
+    st.seq_len.copy_(torch.tensor(lens, dtype=torch.int32))
+    # ragged aging ranges on layer 1, codes zeroed first
+    st.codes[1].zero_()
+    cf = torch.tensor([100, 700], dtype=torch.int32)
+    ct = torch.tensor([140, 705], dtype=torch.int32)
+    st.age(1, cf, ct)
+    torch.cuda.synchronize()
+    _lib.device_status()
+    for b in range(B):
+        for h in range(H):
+            kk = st.cb_k[1, b, h].cpu().numpy()
+            cbk = st.codebook[1, b, h].cpu().numpy()
+            cents = [cbk[s, :kk[s]] for s in range(M)]
+            Kh = st.k[1, b, h].float().cpu().numpy()
+            got = st.codes[1, b, h, :, :M].cpu().numpy()
+            for t in range(int(cf[b]), int(ct[b])):
+                np.testing.assert_array_equal(got[t], O.pq_assign(Kh[t:t + 1], cents)[0], err_msg=f"b{b} h{h} t{t}")
+            assert not got[:int(cf[b])].any() and not got[int(ct[b]):].any(), "codes outside the range changed"
+    # append one token to every layer; the boundary token is aged on every layer
+    for layer in range(2):
+        st.assign(layer, 0, max(lens))
+    rng = np.random.default_rng(5)
+    kn = torch.from_numpy(rng.standard_normal((2, B, H, D)).astype(np.float32)).half().cuda()
+    vn = torch.from_numpy(rng.standard_normal((2, B, H, D)).astype(np.float32)).half().cuda()
+    before = st.codes.clone()
+    st.append(kn, vn, hot_window=hot)
+    torch.cuda.synchronize()
+    _lib.device_status()
+    assert st.seq_len.cpu().tolist() == [n + 1 for n in lens]
+    for layer in range(2):
+        for b in range(B):
+            assert torch.equal(st.k[layer, b, :, lens[b]], kn[layer, b]) and torch.equal(st.v[layer, b, :, lens[b]], vn[layer, b])
+            t = lens[b] - hot
+            for h in range(H):
+                kk = st.cb_k[layer, b, h].cpu().numpy()
+                cbk = st.codebook[layer, b, h].cpu().numpy()
+                cents = [cbk[s, :kk[s]] for s in range(M)]
+                Kh = st.k[layer, b, h].float().cpu().numpy()
+                np.testing.assert_array_equal(st.codes[layer, b, h, t, :M].cpu().numpy(),
+                                              O.pq_assign(Kh[t:t + 1], cents)[0])
+            mask = torch.ones(st.cap, dtype=torch.bool)
+            mask[t] = False
+            assert torch.equal(st.codes[layer, b][:, mask], before[layer, b][:, mask])
+    # the decode at the new length agrees with the oracle
+    Q = O.gen_queries(31, B, H * G, D)
+    q = torch.from_numpy(Q).half().cuda()
+    _check_store(st, q, [n + 1 for n in lens], 0.125, 128, 4, hot, "after append",
+                 exclude_rows={b: {lens[b] - hot} for b in range(B)})
