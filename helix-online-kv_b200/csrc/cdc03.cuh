@@ -1007,6 +1007,14 @@ struct Attn {
   }
 };
 
+constexpr int K7_RANK_MAX = 1024;   // up to this many keys, selection by rank counting
+
+// Rows of the K7 staging tile: K and V rows of up to 128 tokens in 64 KB.
+template <int D, typename KVT>
+__host__ __device__ constexpr int k7_stage_rows() {
+  return (65536 / (2 * D * (int)sizeof(KVT))) < 128 ? (65536 / (2 * D * (int)sizeof(KVT))) : 128;
+}
+
 template <int D, typename KVT>
 __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   using A = AttnGeo<D>;
@@ -1119,19 +1127,51 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
       }
     }
     const int n = s_n;
-    if (n > cr.kp) select_topm<K7_THREADS>(keys, n, cr.kp, hist, &s_sel);
     const int m = min(n, cr.kp);
+    __syncthreads();   // every thread has read s_n
     for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
-    for (int i = tid; i < m; i += K7_THREADS) sel[cr.sink + i] = (int)key_idx(keys[i]);
+    if (n > cr.kp && n <= K7_RANK_MAX) {
+      // few keys: a key is selected when fewer than k' keys beat it (keys are unique)
+      if (tid == 0) s_n = 0;
+      __syncthreads();
+      for (int i = tid; i < n; i += K7_THREADS) {
+        const uint64_t x = keys[i];
+        int rank = 0;
+        for (int j = 0; j < n; ++j) rank += keys[j] > x;
+        if (rank < cr.kp) sel[cr.sink + atomicAdd(&s_n, 1)] = (int)key_idx(x);
+      }
+    } else {
+      if (n > cr.kp) select_topm<K7_THREADS>(keys, n, cr.kp, hist, &s_sel);
+      for (int i = tid; i < m; i += K7_THREADS) sel[cr.sink + i] = (int)key_idx(keys[i]);
+    }
     n_sel = cr.sink + m;
     __syncthreads();
   }
 
-  // ---- exact attention over the selected cold tokens ------------------------
-  at.run(kb, vb, n_sel, warp, scale, [&](int i) { return explicit_sel ? sel[i] : i; },
-         [&](int i, float s) {
-           if (want_scores && at.sl == 0 && i < sel_cap) p.sel_score[sel_base + i] = s;
-         });
+  // ---- exact attention over the selected cold tokens: rows staged in shared
+  // memory by cp.async, a tile of K7_STAGE rows at a time (one memory round
+  // trip per tile instead of one per batch of rows)
+  {
+    const int stage_rows_n = k7_stage_rows<D, KVT>();
+    KVT* sk = reinterpret_cast<KVT*>(part + NW * (D + 2));
+    KVT* sv = sk + (int64_t)stage_rows_n * D;
+    constexpr int C16 = D * (int)sizeof(KVT) / 16;
+    for (int base = 0; base < n_sel; base += stage_rows_n) {
+      const int n = min(stage_rows_n, n_sel - base);
+      for (int i = tid; i < n * 2 * C16; i += K7_THREADS) {
+        const int e = i / (2 * C16), rem = i - e * 2 * C16, kv = rem / C16, ch = rem - kv * C16;
+        const int64_t t = explicit_sel ? sel[base + e] : base + e;
+        cp_async16(reinterpret_cast<unsigned char*>(kv == 0 ? sk : sv) + ((int64_t)e * D) * sizeof(KVT) + ch * 16,
+                   reinterpret_cast<const unsigned char*>((kv == 0 ? kb : vb) + t * D) + ch * 16);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      at.run(sk, sv, n, warp, scale, [&](int i) { return i; }, [&](int i, float s) {
+        if (want_scores && at.sl == 0 && base + i < sel_cap) p.sel_score[sel_base + base + i] = s;
+      });
+      __syncthreads();
+    }
+  }
 
   // combine the SUB token groups of this warp, then the warps
 #pragma unroll
