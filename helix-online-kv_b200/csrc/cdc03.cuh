@@ -1051,9 +1051,31 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   AT at;
   at.init(s_q, lane);
 
+  // rows of tokens tok(0..n) staged in shared memory by cp.async, a tile of
+  // k7_stage_rows at a time (one memory round trip per tile), then attended
+  const int stage_rows_n = k7_stage_rows<D, KVT>();
+  KVT* sk = reinterpret_cast<KVT*>(part + NW * (D + 2));
+  KVT* sv = sk + (int64_t)stage_rows_n * D;
+  auto attend_staged = [&](int n_all, auto tok, auto on_score) {
+    constexpr int C16 = D * (int)sizeof(KVT) / 16;
+    for (int base = 0; base < n_all; base += stage_rows_n) {
+      const int n = min(stage_rows_n, n_all - base);
+      for (int i = tid; i < n * 2 * C16; i += K7_THREADS) {
+        const int e = i / (2 * C16), rem = i - e * 2 * C16, kv = rem / C16, ch = rem - kv * C16;
+        const int64_t t = tok(base + e);
+        cp_async16(reinterpret_cast<unsigned char*>(kv == 0 ? sk : sv) + ((int64_t)e * D) * sizeof(KVT) + ch * 16,
+                   reinterpret_cast<const unsigned char*>((kv == 0 ? kb : vb) + t * D) + ch * 16);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      at.run(sk, sv, n, warp, scale, [&](int i) { return i; }, [&](int i, float s) { on_score(base + i, s); });
+      __syncthreads();
+    }
+  };
+
   // ---- hot window: independent of the candidate stage, done before waiting --
   const int n_hot = cr.S - cr.Sc;
-  at.run(kb, vb, n_hot, warp, scale, [&](int i) { return cr.Sc + i; }, [](int, float) {});
+  attend_staged(n_hot, [&](int i) { return (int64_t)(cr.Sc + i); }, [](int, float) {});
 
   // ---- wait for the candidate stage ------------------------------------------
   pdl_wait();
@@ -1151,27 +1173,9 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   // ---- exact attention over the selected cold tokens: rows staged in shared
   // memory by cp.async, a tile of K7_STAGE rows at a time (one memory round
   // trip per tile instead of one per batch of rows)
-  {
-    const int stage_rows_n = k7_stage_rows<D, KVT>();
-    KVT* sk = reinterpret_cast<KVT*>(part + NW * (D + 2));
-    KVT* sv = sk + (int64_t)stage_rows_n * D;
-    constexpr int C16 = D * (int)sizeof(KVT) / 16;
-    for (int base = 0; base < n_sel; base += stage_rows_n) {
-      const int n = min(stage_rows_n, n_sel - base);
-      for (int i = tid; i < n * 2 * C16; i += K7_THREADS) {
-        const int e = i / (2 * C16), rem = i - e * 2 * C16, kv = rem / C16, ch = rem - kv * C16;
-        const int64_t t = explicit_sel ? sel[base + e] : base + e;
-        cp_async16(reinterpret_cast<unsigned char*>(kv == 0 ? sk : sv) + ((int64_t)e * D) * sizeof(KVT) + ch * 16,
-                   reinterpret_cast<const unsigned char*>((kv == 0 ? kb : vb) + t * D) + ch * 16);
-      }
-      cp_async_wait_all();
-      __syncthreads();
-      at.run(sk, sv, n, warp, scale, [&](int i) { return i; }, [&](int i, float s) {
-        if (want_scores && at.sl == 0 && base + i < sel_cap) p.sel_score[sel_base + base + i] = s;
-      });
-      __syncthreads();
-    }
-  }
+  attend_staged(n_sel, [&](int i) { return (int64_t)(explicit_sel ? sel[i] : i); }, [&](int i, float s) {
+    if (want_scores && at.sl == 0 && i < sel_cap) p.sel_score[sel_base + i] = s;
+  });
 
   // combine the SUB token groups of this warp, then the warps
 #pragma unroll
