@@ -144,3 +144,43 @@ def test_compressed_cache_under_generate():
     rep = cache.memory_report()
     assert rep["exact_bytes"] > 0 and rep["compressed_bytes"] > 0
     assert rep["total_bytes"] == rep["exact_bytes"] + rep["compressed_bytes"]
+
+
+def test_cdc03_attention_in_hf_model():
+    """CDC-03 as the attention implementation of an HF Llama: with a token budget
+    covering the whole cold range a decode step equals exact attention; with
+    top-32 it runs the selection, and the tiers follow the cache lifecycle."""
+    transformers = pytest.importorskip("transformers")
+    from helix_online_kv.cdc03_attention import CDC03Cache
+    from helix_online_kv.config import OnlineKVConfig
+    cfg = transformers.LlamaConfig(vocab_size=256, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=1024)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).cuda().half().eval()
+    model.config._attn_implementation = "sdpa"
+    ids = torch.randint(0, 256, (1, 400), device="cuda")
+
+    def two_steps(cache):
+        with torch.no_grad():
+            out = model(ids, past_key_values=cache, use_cache=True)
+            nxt = out.logits[:, -1:].argmax(-1)
+            out2 = model(nxt, past_key_values=cache, use_cache=True)
+        return out2.logits[0, -1].float()
+
+    ref = two_steps(transformers.DynamicCache())
+    for top_k, exact in ((4096, True), (32, False)):
+        kvc = OnlineKVConfig(calibration_tokens=128, hot_window=64, pq_subspaces=8, exact_layers=[0], top_k=top_k)
+        cache = CDC03Cache(kvc, n_layers=2, batch=1, kv_heads=2, head_dim=64, capacity=1024, dtype=torch.float16)
+        cache.attach(model)
+        got = two_steps(cache)
+        from helix_online_kv import _lib
+        _lib.device_status()
+        model.config._attn_implementation = "sdpa"
+        assert torch.isfinite(got).all()
+        assert cache.ready(1) and not cache.ready(0)
+        assert cache._len[1] == 401 and cache._coded[1] == 401 - 64
+        cos = torch.nn.functional.cosine_similarity(got, ref, dim=0).item()
+        if exact:
+            assert cos > 0.9999 and (got - ref).abs().max().item() < 5e-2, (cos, (got - ref).abs().max().item())
+        else:
+            assert cos > 0.9, cos
