@@ -1073,9 +1073,11 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     }
   };
 
-  // ---- hot window: independent of the candidate stage, done before waiting --
+  // ---- hot window: independent of the candidate stage, done before waiting
+  // (rows straight from memory, 8 in flight per warp: the 256 KB of a staged
+  // hot window would cost two tile round trips)
   const int n_hot = cr.S - cr.Sc;
-  attend_staged(n_hot, [&](int i) { return (int64_t)(cr.Sc + i); }, [](int, float) {});
+  at.run(kb, vb, n_hot, warp, scale, [&](int i) { return cr.Sc + i; }, [](int, float) {});
 
   // ---- wait for the candidate stage ------------------------------------------
   pdl_wait();
