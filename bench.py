@@ -100,6 +100,9 @@ def cpu_rate(n_workers: int, per_worker: int, reps: int, S: int, D: int, M: int,
     """Head-queries/s of the oracle's CDC-03 (numpy) on n_workers processes."""
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
+    # one BLAS thread per worker process (the workers read these when they import numpy)
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"
     jobs = [(1000 + i, per_worker, S, D, M, G, w["top_k"], w["sink_tokens"], w["hot_window"])
             for i in range(n_workers)]
     with ctx.Pool(n_workers) as pool:
@@ -375,11 +378,13 @@ def run_ours(args):
         cents = [cbh[s, :kk[s]] for s in range(M)]
         codes = store.codes[0, 0, 0, :S, :M].cpu().numpy()
         qh = q[0, 0, :Hq // H].float().cpu().numpy()
-        t0 = time.perf_counter()
-        while time.perf_counter() - t0 < args.cpu_seconds:
-            O.cdc03_hot_attention(qh[reps % len(qh)], Kh, Vh, codes, cents, scale, top_k, sink, hot)
-            reps += 1
-        t_cpu = time.perf_counter() - t0
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(limits=1):   # one core: BLAS single-threaded
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < args.cpu_seconds:
+                O.cdc03_hot_attention(qh[reps % len(qh)], Kh, Vh, codes, cents, scale, top_k, sink, hot)
+                reps += 1
+            t_cpu = time.perf_counter() - t0
         hq_s = reps / t_cpu
         cpu = {"value": hq_s / (Ls * Hq), "unit": "tokens/s", "cores": 1, "kind": "port",
                "sample": f"{reps} head-queries (S=16384, D=128, M=16) in {t_cpu:.1f} s on one core, "
