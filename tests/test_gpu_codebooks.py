@@ -168,3 +168,98 @@ def test_codebook_quality_properties():
     assert vq.finalize_calibration()["n_clusters"] <= 50
     with pytest.raises(RuntimeError, match="already finalized"):
         vq.feed_calibration(rng.standard_normal((5, 64)).astype(np.float32))
+
+
+def test_vector_gather_scores_equal_decode_dot():
+    """VectorCodebook: precomputed query scores gathered by index equal the dot
+    products with the decoded vectors (the reference's rtol 1e-5 identity)."""
+    from helix_online_kv.vector_codebook import VectorCodebook
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((600, 64)).astype(np.float32)
+    vq = VectorCodebook(n_clusters=64, head_dim=64)
+    vq.feed_calibration(x[:300])
+    vq.finalize_calibration()
+    idx = vq.assign(x[300:])
+    assert idx.shape == (300,) and idx.dtype == np.uint8
+    q = rng.standard_normal(64).astype(np.float32)
+    got = vq.gather_scores(vq.precompute_query_scores(q), idx)
+    np.testing.assert_allclose(got, vq.decode(idx) @ q, rtol=1e-5, atol=1e-6)
+    with pytest.raises(ValueError, match="Expected shape"):
+        vq.assign(rng.standard_normal((4, 32)).astype(np.float32))
+
+
+@pytest.mark.parametrize("M", [4, 8, 16])
+def test_product_adc_equals_decode_dot(M):
+    """ProductCodebook: [N, M] uint8 codes; ADC scores from the distance tables
+    match the dot with the decoded vectors (rtol 1e-4, atol 1e-5)."""
+    from helix_online_kv.product_codebook import ProductCodebook
+    rng = np.random.default_rng(11 + M)
+    x = rng.standard_normal((800, 64)).astype(np.float32)
+    pq = ProductCodebook(n_subspaces=M, sub_clusters=64, head_dim=64)
+    pq.feed_calibration(x[:400])
+    pq.finalize_calibration()
+    codes = pq.assign(x[400:])
+    assert codes.shape == (400, M) and codes.dtype == np.uint8
+    q = rng.standard_normal(64).astype(np.float32)
+    adc = pq.gather_pq_scores(pq.precompute_distance_tables(q), codes)
+    np.testing.assert_allclose(adc, pq.decode(codes) @ q, rtol=1e-4, atol=1e-5)
+    with pytest.raises(ValueError, match="divisible"):
+        ProductCodebook(n_subspaces=7, head_dim=64)
+
+
+def test_product_beats_vector_quantisation():
+    """At the same codes per subspace, PQ reconstructs better than one VQ codebook."""
+    from helix_online_kv.product_codebook import ProductCodebook
+    from helix_online_kv.vector_codebook import VectorCodebook
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((1500, 64)).astype(np.float32)
+    vq = VectorCodebook(n_clusters=64, head_dim=64)
+    vq.feed_calibration(x[:1000])
+    vq.finalize_calibration()
+    pq = ProductCodebook(n_subspaces=8, sub_clusters=64, head_dim=64)
+    pq.feed_calibration(x[:1000])
+    pq.finalize_calibration()
+    test = x[1000:]
+    assert pq.quantization_error(test, pq.assign(test)) < vq.quantization_error(test, vq.assign(test))
+
+
+def test_scalar_drift_update():
+    """EMA drift correction runs only above the threshold and moves the centroids."""
+    from helix_online_kv.codebook import OnlineCodebook
+    rng = np.random.default_rng(5)
+    cb = OnlineCodebook(n_clusters=16)
+    cb.feed_calibration(rng.standard_normal(4000).astype(np.float32))
+    cb.finalize_calibration()
+    before = cb.centroids.copy()
+    assert not cb.maybe_update_centroids(rng.standard_normal(100).astype(np.float32), error=0.0)
+    np.testing.assert_array_equal(cb.centroids, before)
+    shifted = (rng.standard_normal(4000) + 3.0).astype(np.float32)
+    assert cb.maybe_update_centroids(shifted, error=1.0)
+    assert not np.array_equal(cb.centroids, before)
+    assert cb.centroids.mean() > before.mean()
+
+
+def test_layer_state_lifecycle():
+    """KVLayerState: phase change at exactly calibration_tokens, compressed
+    count, decoded tokens close to the originals, memory accounting."""
+    from helix_online_kv.config import OnlineKVConfig
+    from helix_online_kv.layer_state import KVLayerState
+    rng = np.random.default_rng(17)
+    cfg = OnlineKVConfig(calibration_tokens=32, exact_layers=[0])
+    ls = KVLayerState(1, cfg)
+    dim = 2 * 64
+    toks = rng.standard_normal((80, 2, dim)).astype(np.float32)
+    for i in range(32):
+        assert ls.is_calibrating
+        ls.feed_token(toks[i, 0], toks[i, 1])
+    assert ls.is_streaming and ls.compressed_token_count == 0
+    for i in range(32, 80):
+        ls.feed_token(toks[i, 0], toks[i, 1])
+    assert ls.compressed_token_count == 48 and ls.tokens_seen == 80
+    k, v = ls.get_compressed_kv(10)
+    kt = np.asarray(k.cpu() if hasattr(k, "cpu") else k, dtype=np.float32)
+    cos = float(kt @ toks[42, 0] / (np.linalg.norm(kt) * np.linalg.norm(toks[42, 0])))
+    assert cos > 0.99
+    mem = ls.memory_bytes()
+    assert mem["index_bytes"] == 48 * 2 * dim and mem["total_bytes"] == mem["codebook_bytes"] + mem["index_bytes"]
+    assert KVLayerState(0, cfg).memory_bytes()["total_bytes"] == 0
