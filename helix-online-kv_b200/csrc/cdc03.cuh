@@ -35,7 +35,7 @@ constexpr int K6_THREADS = 256;
 
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
-constexpr int K7_CAP = 2048;         // key buffer of the exact selection
+constexpr int K7_CAP = 1024;         // key buffer of the exact selection (rank counting)
 constexpr int TOPK_MAX = 1024;       // largest top_k with k < S_c
 constexpr int MAX_CHUNKS = 512;      // K6 chunks per (sequence, KV head)
 
@@ -804,111 +804,6 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   if (tid < GT) cnt_out[tid] = (tid < p.G && s_cnt[tid] > CAND_MAX) ? -1 : (tid < p.G ? s_cnt[tid] : 0);
 }
 
-// ---------------------------------------------------------------------------
-// Block-wide exact selection: keep the m largest of n unique 64-bit keys in
-// keys[0..m).  Histogram refinement on the key range; each round narrows the
-// range containing the m-th key by >= 2^9, so it ends in <= 8 rounds.
-// ---------------------------------------------------------------------------
-struct SelShared {
-  unsigned long long lo, hi, thr;
-  int need, done, bstar, above, binc, n_out;
-};
-
-template <int NT>
-__device__ void select_topm(uint64_t* keys, int n, int m, uint32_t* hist, SelShared* sh) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NW = NT / 32;
-  __shared__ unsigned long long red_lo[NW], red_hi[NW];
-  if (n <= m) return;
-  unsigned long long lo = ~0ull, hi = 0ull;
-  for (int i = tid; i < n; i += NT) { unsigned long long k = keys[i]; lo = k < lo ? k : lo; hi = k > hi ? k : hi; }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    unsigned long long a = __shfl_xor_sync(0xffffffffu, lo, o), c = __shfl_xor_sync(0xffffffffu, hi, o);
-    lo = a < lo ? a : lo; hi = c > hi ? c : hi;
-  }
-  if (lane == 0) { red_lo[warp] = lo; red_hi[warp] = hi; }
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long L = red_lo[0], H = red_hi[0];
-    for (int w = 1; w < NW; ++w) { L = red_lo[w] < L ? red_lo[w] : L; H = red_hi[w] > H ? red_hi[w] : H; }
-    sh->lo = L; sh->hi = H; sh->need = m; sh->done = 0;
-  }
-  __syncthreads();
-  for (int round = 0; round < 10; ++round) {
-    const unsigned long long L = sh->lo, H = sh->hi;
-    const unsigned long long range = H - L;
-    const int bits = range ? 64 - __clzll((long long)range) : 0;
-    const int shift = bits > 10 ? bits - 10 : 0;
-    const int nb = (int)(range >> shift) + 1;
-    for (int i = tid; i < nb; i += NT) hist[i] = 0;
-    __syncthreads();
-    for (int i = tid; i < n; i += NT) {
-      const unsigned long long k = keys[i];
-      if (k >= L && k <= H) atomicAdd(&hist[(int)((k - L) >> shift)], 1u);
-    }
-    __syncthreads();
-    if (warp == 0) {
-      const int need = sh->need;
-      uint32_t ls = 0;
-      for (int i = 0; i < 32; ++i) { int bb = lane * 32 + i; if (bb < nb) ls += hist[bb]; }
-      uint32_t suf = ls;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-        if (lane + o < 32) suf += t;
-      }
-      const unsigned ball = __ballot_sync(0xffffffffu, suf >= (uint32_t)need);
-      const int lstar = ball ? 31 - __clz((int)ball) : 0;
-      const uint32_t above0 = __shfl_sync(0xffffffffu, suf - ls, lstar);
-      if (lane == lstar) {
-        uint32_t cum = above0;
-        int bs = lane * 32, ab = (int)above0, bc = 0;
-        for (int i = 31; i >= 0; --i) {
-          int bb = lane * 32 + i;
-          if (bb >= nb) continue;
-          if (cum + hist[bb] >= (uint32_t)need) { bs = bb; ab = (int)cum; bc = (int)hist[bb]; break; }
-          cum += hist[bb];
-        }
-        sh->bstar = bs; sh->above = ab; sh->binc = bc;
-        const unsigned long long nlo = L + ((unsigned long long)bs << shift);
-        const int nneed = need - ab;
-        if (bc == nneed || shift == 0) {
-          sh->thr = nlo; sh->done = 1;
-        } else {
-          unsigned long long nhi = nlo + ((1ull << shift) - 1ull);
-          sh->lo = nlo; sh->hi = nhi < H ? nhi : H; sh->need = nneed;
-        }
-      }
-    }
-    __syncthreads();
-    if (sh->done) break;
-  }
-  if (!sh->done) { if (tid == 0) { sh->thr = sh->lo; dev_flag(HOKV_ERR_TIMEOUT); } }
-  __syncthreads();
-  const unsigned long long thr = sh->thr;
-  constexpr int PER = K7_CAP / NT;
-  unsigned long long mine[PER];
-  bool take[PER];
-#pragma unroll
-  for (int r = 0; r < PER; ++r) {
-    const int i = tid + r * NT;
-    take[r] = false;
-    mine[r] = 0ull;
-    if (i < n) { mine[r] = keys[i]; take[r] = mine[r] >= thr; }
-  }
-  if (tid == 0) sh->n_out = 0;
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < PER; ++r) {
-    if (take[r]) {
-      int slot = atomicAdd(&sh->n_out, 1);
-      if (slot < m) keys[slot] = mine[r];
-    }
-  }
-  __syncthreads();
-}
-
 template <int D>
 struct AttnGeo {
   static constexpr int DPL = (D <= 128) ? 4 : D / 32;   // dims per lane
@@ -1007,12 +902,20 @@ struct Attn {
   }
 };
 
-constexpr int K7_RANK_MAX = 1024;   // up to this many keys, selection by rank counting
+constexpr int K7_RANK_MAX = K7_CAP;   // up to this many keys, selection by rank counting
+static_assert(K7_THREADS == 256, "k7_select_attend clears a 256-bin histogram with one thread per bin");
 
 // Rows of the K7 staging tile: K and V rows of up to 128 tokens in 64 KB.
 template <int D, typename KVT>
 __host__ __device__ constexpr int k7_stage_rows() {
   return (65536 / (2 * D * (int)sizeof(KVT))) < 128 ? (65536 / (2 * D * (int)sizeof(KVT))) : 128;
+}
+// Bytes of the staging space: the tile, and at least 64 KB (it also caches the
+// selection keys of long contexts).
+template <int D, typename KVT>
+__host__ __device__ constexpr int k7_stage_bytes() {
+  return 2 * k7_stage_rows<D, KVT>() * D * (int)sizeof(KVT) > 65536 ? 2 * k7_stage_rows<D, KVT>() * D * (int)sizeof(KVT)
+                                                                      : 65536;
 }
 
 template <int D, typename KVT>
@@ -1023,12 +926,11 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* T = reinterpret_cast<float*>(smem);                                 // [M][256] exact sub-table
   uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.M * 1024);           // [K7_CAP]
-  uint32_t* hist = reinterpret_cast<uint32_t*>(keys + K7_CAP);               // [1024]
-  int* sel = reinterpret_cast<int*>(hist + 1024);                            // [TOPK_MAX]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(keys + K7_CAP);               // [256]
+  int* sel = reinterpret_cast<int*>(hist + 256);                             // [TOPK_MAX]
   float* part = reinterpret_cast<float*>(sel + TOPK_MAX);                    // [NW][D + 2]
   __shared__ float s_q[D];
   __shared__ int s_n, s_over, s_cnt[MAX_CHUNKS], s_off[MAX_CHUNKS + 1];
-  __shared__ SelShared s_sel;
 
   const int Hq = p.Hkv * p.G;
   const int u = blockIdx.x / p.G, g = blockIdx.x - (blockIdx.x / p.G) * p.G;
@@ -1106,69 +1008,160 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
       for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
     }
     const int n_listed = s_off[p.n_chunks];
-    // listed candidates: selection keys (exact scores) written by the candidate stage
-    for (int base = 0; base < n_listed; base += K7_CAP / 2) {
-      if (s_n + K7_CAP / 2 > K7_CAP) {
-        select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
-        if (tid == 0) s_n = min(s_n, cr.kp);
-        __syncthreads();
-      }
-      const int nb = min(K7_CAP / 2, n_listed - base);
-      for (int i = tid; i < nb; i += K7_THREADS) {
-        const int li = base + i;
+    for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
+    if (!s_over && n_listed <= K7_RANK_MAX) {
+      // few keys: gathered into shared memory; a key is selected when fewer
+      // than k' keys beat it (keys are unique)
+      for (int li = tid; li < n_listed; li += K7_THREADS) {
         int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
         while (lo < hi) {
           const int mid = (lo + hi + 1) >> 1;
           if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
         }
-        keys[s_n + i] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
+        keys[li] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
       }
-      __syncthreads();
-      if (tid == 0) s_n += nb;
-      __syncthreads();
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    // overflowed chunks: rescan every non-sink token of the chunk
-    const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
-    for (int c = 0; c < p.n_chunks; ++c) {
-      if (s_cnt[c] >= 0) continue;
-      const int clo = max(c * p.chunk, cr.sink), chi = min((c + 1) * p.chunk, cr.Sc);
-      for (int base = clo; base < chi; base += K7_THREADS) {
-        if (s_n + K7_THREADS > K7_CAP) {
-          select_topm<K7_THREADS>(keys, s_n, cr.kp, hist, &s_sel);
-          if (tid == 0) s_n = min(s_n, cr.kp);
-          __syncthreads();
-        }
-        const int t = base + tid;
-        if (t < chi) {
-          const uint8_t* row = codes + (int64_t)t * p.CS;
-          float sum = 0.f;
-          for (int s = 0; s < M; ++s) sum = fadd(sum, T[s * 256 + row[s]]);
-          keys[atomicAdd(&s_n, 1)] = sel_key(fmul(sum, scale), (uint32_t)t);
-        }
-        __syncthreads();
-      }
-    }
-    const int n = s_n;
-    const int m = min(n, cr.kp);
-    __syncthreads();   // every thread has read s_n
-    for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
-    if (n > cr.kp && n <= K7_RANK_MAX) {
-      // few keys: a key is selected when fewer than k' keys beat it (keys are unique)
       if (tid == 0) s_n = 0;
       __syncthreads();
-      for (int i = tid; i < n; i += K7_THREADS) {
+      for (int i = tid; i < n_listed; i += K7_THREADS) {
         const uint64_t x = keys[i];
         int rank = 0;
-        for (int j = 0; j < n; ++j) rank += keys[j] > x;
+        for (int j = 0; j < n_listed; ++j) rank += keys[j] > x;
         if (rank < cr.kp) sel[cr.sink + atomicAdd(&s_n, 1)] = (int)key_idx(x);
       }
     } else {
-      if (n > cr.kp) select_topm<K7_THREADS>(keys, n, cr.kp, hist, &s_sel);
-      for (int i = tid; i < m; i += K7_THREADS) sel[cr.sink + i] = (int)key_idx(keys[i]);
+      // many keys (chunk-local thresholds of long contexts) or overflowed
+      // lists: radix select of the k'-th largest key, 8 bits a round, over the
+      // listed keys and the exact keys of every token of an overflowed chunk
+      // (recomputed each round from the exact sub-table); the selection is
+      // exactly the keys >= that key
+      cp_async_wait_all();
+      const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
+      __shared__ int s_ooff[MAX_CHUNKS], s_nall;   // overflowed chunks: key positions after the listed keys
+      auto for_each_source_key = [&](auto fn) {
+        // listed keys: flat index, 8 loads in flight per thread
+        constexpr int UK = 8;
+        for (int base = tid; base < n_listed; base += UK * K7_THREADS) {
+          uint64_t kk[UK];
+#pragma unroll
+          for (int r = 0; r < UK; ++r) {
+            const int li = base + r * K7_THREADS;
+            kk[r] = 0ull;
+            if (li < n_listed) {
+              int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
+              while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
+              }
+              kk[r] = __ldcg(p.cand_key + (cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo]));
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < UK; ++r)
+            if (base + r * K7_THREADS < n_listed) fn(kk[r], base + r * K7_THREADS);
+        }
+        // overflowed chunks: exact keys of every non-sink token
+        for (int c = 0; c < p.n_chunks; ++c) {
+          if (s_cnt[c] >= 0) {
+            continue;
+          } else {
+            const int clo = max(c * p.chunk, cr.sink), chi = min((c + 1) * p.chunk, cr.Sc);
+            for (int t = clo + tid; t < chi; t += K7_THREADS) {
+              const uint32_t* row = reinterpret_cast<const uint32_t*>(codes + (int64_t)t * p.CS);
+              uint32_t cw[8];
+#pragma unroll
+              for (int w = 0; w < 8; ++w) cw[w] = (w < p.CS / 4) ? __ldg(row + w) : 0u;   // one row, loads in flight together
+              float sum = 0.f;
+              for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[s2 * 256 + ((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu)]);
+              fn(sel_key(fmul(sum, scale), (uint32_t)t), n_listed + s_ooff[c] + (t - clo));
+            }
+          }
+        }
+      };
+      // every key once into the (idle) row staging space when they fit there
+      if (tid == 0) {
+        int acc = 0;
+        for (int c = 0; c < p.n_chunks; ++c) {
+          s_ooff[c] = acc;
+          if (s_cnt[c] < 0) acc += max(0, min((c + 1) * p.chunk, cr.Sc) - max(c * p.chunk, cr.sink));
+        }
+        s_nall = n_listed + acc;
+      }
+      __syncthreads();
+      uint64_t* kc = reinterpret_cast<uint64_t*>(sk);
+      const int kc_cap = k7_stage_bytes<D, KVT>() / 8;
+      const bool cached = s_nall <= kc_cap;
+      if (cached) {
+        for_each_source_key([&](uint64_t key, int pos) { kc[pos] = key; });
+        __syncthreads();
+      }
+      auto for_each_key = [&](auto fn) {
+        if (cached) {
+          for (int i = tid; i < s_nall; i += K7_THREADS) fn(kc[i]);
+        } else {
+          for_each_source_key([&](uint64_t key, int) { fn(key); });
+        }
+      };
+      __shared__ unsigned long long s_pre, s_msk;
+      __shared__ int s_need, s_done;
+      if (tid == 0) { s_pre = 0ull; s_msk = 0ull; s_need = cr.kp; s_done = 0; }
+      __syncthreads();
+      for (int shift = 56; shift >= 0; shift -= 8) {
+        if (s_done) break;   // uniform: read after a barrier
+        hist[tid] = 0;       // K7_THREADS == 256 bins
+        __syncthreads();
+        const unsigned long long pre = s_pre, msk = s_msk;
+        for_each_key([&](uint64_t key) {
+          if ((key & msk) == pre) atomicAdd(&hist[(int)((key >> shift) & 255u)], 1u);
+        });
+        __syncthreads();
+        if (warp == 0) {
+          const int need = s_need;
+          uint32_t ls = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ls += hist[lane * 8 + i];
+          uint32_t suf = ls;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+            if (lane + o < 32) suf += t;
+          }
+          const unsigned ball = __ballot_sync(0xffffffffu, suf >= (uint32_t)need);
+          if (ball == 0u) {
+            if (lane == 0) s_done = 1;   // fewer matching keys than needed: take them all
+          } else {
+            const int lstar = 31 - __clz((int)ball);
+            if (lane == lstar) {
+              uint32_t cum = suf - ls;
+              for (int i = 7; i >= 0; --i) {
+                const int d = lane * 8 + i;
+                const uint32_t hd = hist[d];
+                if (cum + hd >= (uint32_t)need) {
+                  const int rest = need - (int)cum;
+                  s_pre = pre | ((unsigned long long)d << shift);
+                  s_msk = msk | (255ull << shift);
+                  s_need = rest;
+                  if ((int)hd == rest || shift == 0) s_done = 1;
+                  break;
+                }
+                cum += hd;
+              }
+            }
+          }
+        }
+        __syncthreads();
+      }
+      if (tid == 0) s_n = 0;
+      __syncthreads();
+      const unsigned long long thr = s_pre;
+      for_each_key([&](uint64_t key) {
+        if (key >= thr) {
+          const int slot = atomicAdd(&s_n, 1);
+          if (slot < cr.kp) sel[cr.sink + slot] = (int)key_idx(key);
+        }
+      });
     }
-    n_sel = cr.sink + m;
+    __syncthreads();
+    n_sel = cr.sink + min(s_n, cr.kp);
     __syncthreads();
   }
 

@@ -142,8 +142,8 @@ static int qimg_bytes_for(int CS, int GT) {
 // Stage 2: K7, programmatic launch (hot-window attention overlaps K6).
 template <int D, typename KVT>
 static int launch_k7(const Cdc03P& p, cudaStream_t st) {
-  const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 4096 + (size_t)TOPK_MAX * 4 +
-                    (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)2 * k7_stage_rows<D, KVT>() * D * sizeof(KVT);
+  const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
+                    (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)k7_stage_bytes<D, KVT>();
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
   return launch_ex(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
                    "k7_select_attend", true);

@@ -189,6 +189,13 @@ def test_store_long_context_20k_chunk_thresholds():
     assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "20k") <= 4
 
 
+def test_store_long_context_64k_streamed_selection():
+    """64K tokens: 32 chunks rank alone, so thousands of candidate keys reach
+    the selection, which then runs as a radix select over the candidate lists."""
+    st, q, lens = _store(1, 1, 2, 64, 65536, 8, torch.float16, seed=19)
+    assert _check_store(st, q, lens, 0.125, 128, 4, 256, "64k") <= 4
+
+
 def test_store_group_of_three_uneven_cluster():
     """G = 3 query heads per KV head (one padded score lane) and 3 chunks per
     unit, so the cluster splits 4 subspace groups unevenly over 3 CTAs."""
