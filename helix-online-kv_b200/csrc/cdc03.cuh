@@ -1,25 +1,20 @@
 // cdc03.cuh -- PQ lookup tables, ADC scoring and CDC-03 decode attention.
 //
-// Decode step, per layer, three kernels chained with programmatic dependent
-// launch (each starts its independent prologue while the previous one runs):
-//   K5 k5_tables    grid (B*H_kv): per (sequence, KV head), the exact fp32
-//      sub-tables T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads of
-//      the GQA group (BLAS order), and their quantised image: codes of
-//      floor(65535 / M) levels packed in 16-bit lanes, laid out so that every
-//      shared-memory lookup of K6 is bank-conflict free.
-//   K6 k6_candidates  grid (chunks, B*H_kv): streams the uint8 PQ codes of one
-//      2048-token chunk of cold tokens straight into registers (the first half
-//      is loaded while K5 runs), sums quantised table entries per token in
-//      integer lanes, finds a lower bound of the k'-th largest approximate
-//      score and emits every token whose score lies within the proven error
-//      band of it (index + code row).  Up to 8 chunks of one (sequence, KV
-//      head) form a thread-block cluster and pool their score histograms
-//      through distributed shared memory, so the bound is the unit's own;
-//      longer contexts use each chunk's own (a looser, still valid bound).
+// Decode step, per layer, two kernels chained with programmatic dependent
+// launch (K7 starts its hot-window attention while K6 runs):
+//   K6 k6_candidates  grid (min(chunks, 8), B*H_kv), one thread-block cluster
+//      per (sequence, KV head): the CTAs build the exact fp32 sub-tables
+//      T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads of the GQA
+//      group (BLAS order) and their quantised image (codes of floor(65535 / M)
+//      levels in 16-bit lanes, laid out so every shared-memory lookup is bank
+//      conflict free); each CTA streams the uint8 PQ codes of its 2048-token
+//      chunks into registers, sums quantised entries per token in integer
+//      lanes, pools a score histogram over the cluster, and emits every token
+//      whose score lies within the proven error band of the unit's k'-th
+//      score, rescored exactly (reference summation order) into a selection key.
 //   K7 k7_select_attend  grid (B*H_kv*G): attends the hot window before it
-//      waits for K6, then rescores the candidates exactly in the reference's
-//      summation order, selects sinks + top-(k - sinks) (ties to the lower
-//      token index) and finishes softmax attention over them.
+//      waits for K6, selects sinks + top-(k - sinks) of the candidate keys
+//      (ties to the lower token index) and finishes softmax attention over them.
 //
 // Reference: helix_online_kv/compressed_attention.py:315-412 (hybrid_pq_attention),
 // product_codebook.py:172-227 (tables, gather).
@@ -30,7 +25,6 @@
 
 namespace hokv {
 
-constexpr int K5_THREADS = 256;
 constexpr int K6_THREADS = 256;
 
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
@@ -55,9 +49,9 @@ struct Cdc03P {
   // workspace
   uint64_t* cand_key;     // [units][chunks][GT][CAND_MAX] selection keys of listed candidates (K6 -> K7)
   int* cand_cnt;          // [units][chunks][GT]   listed count, -1 when the list overflowed
-  unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (K5 -> K6)
-  float* texact;          // [units][GT][CS][256]    exact sub-tables (K5 -> K7)
-  int* margin;            // [units][GT]             error band in code units (K5 -> K6)
+  unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (exchanged in the cluster)
+  float* texact;          // [units][GT][CS][256]    exact sub-tables (K6 rescoring, K7 rescans)
+  int* margin;            // [units][GT]             error band in code units
   int n_chunks, chunk, GT, qimg_bytes;
 };
 
@@ -87,23 +81,6 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 // Block until the previous kernel in the stream has completed and its writes are visible.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-
-// Rows [0, lim) of every subspace of one (sequence, KV head) codebook are
-// staged in shared memory as stage[s][j][sd]; lim keeps the stage <= 64 KB.
-__host__ __device__ __forceinline__ int stage_rows(int slots, int covered_dims) {
-  const int lim = 16384 / covered_dims;
-  return slots < lim ? slots : lim;
-}
-
-__device__ __forceinline__ void stage_codebook(float* stage, const float* cb, int M, int slots, int sd, int lim,
-                                               int tid, int nthreads) {
-  const int per_s = lim * sd / 4;  // 16-byte pieces per subspace (sd % 4 == 0)
-  const int total = M * per_s;
-  for (int i = tid; i < total; i += nthreads) {
-    const int s = i / per_s, r = i - s * per_s;
-    cp_async16(stage + (int64_t)s * lim * sd + r * 4, cb + (int64_t)s * slots * sd + r * 4);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Quantised sub-table geometry.  One entry holds the codes of the GT query
@@ -179,17 +156,10 @@ __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
   for (int i = 0; i < W; ++i) w[i] = t[i];
 }
 
-// ===========================================================================
-// K5: exact and quantised sub-tables, one CTA (256 threads) per (b, KV head,
-// query head g).  The centroid rows are staged in shared memory; thread t
-// owns centroid j = t % kpad of the subspaces s = t / kpad + i * (256 / kpad),
-// kpad = the centroid count rounded up to a power of two >= 32, so the CTA
-// runs max(1, 256 / kpad) subspaces at a time.  Each CTA writes its head's
-// 16-bit lane of the packed entries, its exact fp32 table and its margin.
-// ===========================================================================
+// Exact sub-table entry: the GEMV order of NumPy/OpenBLAS for (1 x SD) @ (SD x k)
+// (hokv_math.cuh), so the value equals the reference's bit for bit.
 template <int SD>
 __device__ __forceinline__ float lut_dot(const float* q, const float* c) {
-  // GEMV order of NumPy/OpenBLAS for (1 x SD) @ (SD x k); see hokv_math.cuh
   return dot_gemv(q, c, SD);
 }
 
@@ -226,135 +196,13 @@ __device__ __forceinline__ uint16_t quant_code(float t, float lo, float inv, int
   return (uint16_t)x;
 }
 
-template <int CS, int GT, int SD>
-__device__ __forceinline__ void k5_body(const Cdc03P& p, unsigned char* smem) {
-  using Q = QGeo<CS, GT>;
-  float* stage = reinterpret_cast<float*>(smem);               // <= 64 KB
-  __shared__ float sq[256];
-  __shared__ unsigned s_lo[CS], s_hi[CS];
-  __shared__ float s_lof[CS], s_hif[CS], s_inv;
-  __shared__ int s_k[32], s_kmax;
-
-  const int u = blockIdx.x, g = blockIdx.y;
-  const int b = u / p.Hkv, h = u - b * p.Hkv;
-  const int tid = threadIdx.x, lane = tid & 31;
-  const ColdRange cr = cold_range(p, b);
-  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking needed for this sequence
-  const int D = p.D, M = p.M;
-  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  const int lim = stage_rows(p.slots, M * SD);
-  stage_codebook(stage, cbase, M, p.slots, SD, lim, tid, blockDim.x);
-  const bool real = g < p.G;
-  for (int d = tid; d < D; d += blockDim.x)
-    sq[d] = real ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * D + d) : 0.f;
-  if (tid < M) {
-    const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
-    s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-  }
-  if (tid < CS) { s_lo[tid] = 0xffffffffu; s_hi[tid] = 0u; }
-  cp_async_wait_all();
-  __syncthreads();
-  if (tid == 0) {
-    int km = 1;
-    for (int s = 0; s < M; ++s) km = max(km, s_k[s]);
-    s_kmax = km;
-  }
-  __syncthreads();
-  int kpad = 32;
-  while (kpad < s_kmax) kpad <<= 1;
-  const int groups = 256 / kpad;            // subspaces processed together
-  const int j = tid % kpad, grp = tid / kpad;
-  constexpr int SPT = CS;                    // upper bound of subspaces per thread
-  float tv[SPT];
-  float qs[SD];
-#pragma unroll
-  for (int i = 0; i < SPT; ++i) {
-    const int s = grp + i * groups;
-    tv[i] = 0.f;
-    if (s < M) {   // uniform within a warp: kpad >= 32
-#pragma unroll
-      for (int d = 0; d < SD; ++d) qs[d] = sq[s * SD + d];
-      if (j < s_k[s]) {
-        const float* row = (j < lim) ? stage + ((int64_t)s * lim + j) * SD : cbase + ((int64_t)s * p.slots + j) * SD;
-        float c[SD];
-#pragma unroll
-        for (int d = 0; d < SD; ++d) c[d] = row[d];
-        tv[i] = lut_dot<SD>(qs, c);
-      }
-      const unsigned o = ord_f32(tv[i]);
-      const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
-      if (lane == 0) { atomicMin(&s_lo[s], mn); atomicMax(&s_hi[s], mx); }
-    }
-  }
-  __syncthreads();
-  const int qmax = qmax_for(M);
-  if (tid == 0) {
-    for (int s = 0; s < M; ++s) {
-      float lo = unord_f32(s_lo[s]), hi = unord_f32(s_hi[s]);
-      if (s_k[s] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
-      s_lof[s] = lo;
-      s_hif[s] = hi;
-    }
-    const QuantScale qs = quant_scale(s_lof, s_hif, M, p.scale);
-    s_inv = qs.inv;
-    p.margin[(int64_t)u * GT + g] = qs.margin;
-  }
-  __syncthreads();
-  // 16-bit lane of head g inside an entry: GT <= 2 -> u32 entry, lane g;
-  // GT = 4 -> {h0|h2, h1|h3}; GT = 8 -> {h0|h2, h1|h3, h4|h6, h5|h7}.
-  const int lane16 = (GT <= 2) ? g : ((g >> 2) * 4 + (g & 1) * 2 + ((g & 2) >> 1));
-  uint16_t* img = reinterpret_cast<uint16_t*>(p.qimg + (int64_t)u * p.qimg_bytes);
-  float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
-  const float inv = s_inv;
-#pragma unroll
-  for (int i = 0; i < SPT; ++i) {
-    const int s = grp + i * groups;
-    if (s >= M) continue;
-    // entries j >= kpad (never touched by the stream for valid codes) hold T = 0
-    for (int jj = j; jj < 256; jj += kpad) {
-      const float t = (jj == j) ? tv[i] : 0.f;
-      if (jj == j) tex[s * 256 + jj] = t;
-      else tex[s * 256 + jj] = 0.f;
-      const uint16_t code = quant_code(t, s_lof[s], inv, qmax);
-      for (int copy = 0; copy < Q::NC; ++copy) {
-        const int e = (Q::rb_of(s) * 256 + jj) * Q::COLS + copy * CS + (s % Q::COLS);
-        if constexpr (GT == 1) reinterpret_cast<uint32_t*>(img)[e] = code;   // upper lane stays zero
-        else img[(int64_t)e * (Q::EW / 2) + lane16] = code;
-      }
-    }
-  }
-  // padded subspaces s in [M, CS) contribute nothing: zero their entries once
-  if (g == 0 && M < CS) {
-    for (int i = tid; i < (CS - M) * 256; i += blockDim.x) {
-      const int s = M + i / 256, jj = i % 256;
-      for (int copy = 0; copy < Q::NC; ++copy) {
-        const int e = (Q::rb_of(s) * 256 + jj) * Q::COLS + copy * CS + (s % Q::COLS);
-        for (int l = 0; l < Q::EW / 2; ++l) img[(int64_t)e * (Q::EW / 2) + l] = 0;
-      }
-    }
-  }
-}
-
-template <int CS, int GT>
-__global__ void __launch_bounds__(K5_THREADS) k5_tables(Cdc03P p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  pdl_launch_dependents();
-  switch (p.sd) {
-    case 4: k5_body<CS, GT, 4>(p, smem); break;
-    case 8: k5_body<CS, GT, 8>(p, smem); break;
-    case 16: k5_body<CS, GT, 16>(p, smem); break;
-    case 32: k5_body<CS, GT, 32>(p, smem); break;
-    default: dev_flag(HOKV_ERR_DEVICE_INPUT);
-  }
-}
-
 // ===========================================================================
-// K6: candidate stream, grid (chunks, B*H_kv), 256 threads, 8 tokens per
-// thread.  FUSED (up to 8 chunks per unit): the chunks of one (b, KV head)
-// form a thread-block cluster that builds the unit's tables itself (each CTA
-// one block of subspaces, exchanged through distributed shared memory) and
-// pools its score histograms, so the threshold is the unit-wide k'-th score.
-// Otherwise K5 has built the tables and each chunk uses its own threshold.
+// K6: candidate stream, grid (min(chunks, 8), B*H_kv), 256 threads, 8 tokens
+// of a 2048-token chunk per thread.  The CTAs of one (b, KV head) form a
+// thread-block cluster that builds the unit's tables itself (each CTA one
+// block of subspaces; ranges exchanged through distributed shared memory, the
+// quantised image through L2) and pools its score histograms, so the
+// threshold is the unit-wide k'-th score at any context length.
 // ===========================================================================
 constexpr int K6_TPT = 8;
 constexpr int K6_CHUNK = K6_THREADS * K6_TPT;   // 2048 tokens
@@ -501,38 +349,39 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
   }
 }
 
-template <int CS, int GT, bool FUSED>
+// Chunk c of the unit is handled by CTA c % R of the cluster (R <= 8).  With
+// one chunk per CTA its scores stay in registers between the histogram and the
+// candidate list; with more (long contexts) the CTA scores its chunks twice:
+// once for the histogram, once, after the unit-wide threshold, for the list.
+template <int CS, int GT>
 __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candidates(Cdc03P p) {
   using Q = QGeo<CS, GT>;
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* qlut = smem;                                              // Q::BYTES
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES);           // [GT][HWORDS]
-  uint32_t* full = FUSED ? hist + GT * HWORDS : hist;                      // [GT][HWORDS] pooled
+  uint32_t* full = hist + GT * HWORDS;                                     // [GT][HWORDS] pooled
   __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_nl[GT];
 
   pdl_launch_dependents();
-  const int u = blockIdx.y, c = blockIdx.x;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int R = (int)cl.num_blocks(), me = (int)cl.block_rank();
+  const int u = blockIdx.y;
   const int b = u / p.Hkv, h = u - b * p.Hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ColdRange cr = cold_range(p, b);
-  int* cnt_out = p.cand_cnt + ((int64_t)u * p.n_chunks + c) * GT;
-  if (cr.k >= cr.Sc || cr.kp <= 0) {      // the same for every chunk of the unit
-    if (tid < GT) cnt_out[tid] = 0;
-    return;
-  }
-  const int t0 = c * K6_CHUNK;
-  const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
-  if (!FUSED && lo_t >= hi_t) {
-    if (tid < GT) cnt_out[tid] = 0;
+  const int n_mine = (p.n_chunks - me + R - 1) / R;   // chunks me, me + R, ...
+  if (cr.k >= cr.Sc || cr.kp <= 0) {      // the same for every CTA of the unit
+    for (int i = 0; i < n_mine; ++i)
+      if (tid < GT) p.cand_cnt[((int64_t)u * p.n_chunks + me + i * R) * GT + tid] = 0;
     return;
   }
   const int M = p.M;
   const uint8_t* gcodes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
   constexpr int HT = K6_TPT / 2;
   uint32_t w[HT][Q::W];
-  [[maybe_unused]] int R = 1, me = 0;
-
-  if constexpr (FUSED) {
+  const int c0 = me;
+  {
     // ---- tables built by the cluster: each CTA computes a block of subspaces
     // (whole 16-byte groups of the image), the ranges go to every CTA through
     // distributed shared memory, the quantised entries to the unit's image in
@@ -540,12 +389,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
     __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
     __shared__ int s_k[32];
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    R = (int)cl.num_blocks();
-    me = (int)cl.block_rank();
     cluster_arrive_relaxed();   // phase A: this CTA runs
-    {   // codes of this chunk into L2 while the tables are built
+    for (int i = 0; i < n_mine; ++i) {   // this CTA's codes into L2 while the tables are built
+      const int t0 = (me + i * R) * K6_CHUNK;
       const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
       for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
@@ -640,8 +486,8 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     }
     cluster_arrive();           // phase C: the image is complete in memory
 #pragma unroll
-    for (int it = 0; it < HT; ++it) {
-      const int t = t0 + it * K6_THREADS + tid;
+    for (int it = 0; it < HT; ++it) {   // first codes of the first chunk meanwhile
+      const int t = c0 * K6_CHUNK + it * K6_THREADS + tid;
       if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
       else {
 #pragma unroll
@@ -652,30 +498,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
     cp_async_wait_all();
     __syncthreads();
-  } else {
-    // ---- first half of this thread's codes, loaded before waiting for K5 -----
-#pragma unroll
-    for (int it = 0; it < HT; ++it) {
-      const int t = t0 + it * K6_THREADS + tid;
-      if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
-      else {
-#pragma unroll
-        for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
-      }
-    }
-    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
-    if (tid < GT) s_cnt[tid] = 0;
-    pdl_wait();
-    {
-      const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-      for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
-    }
-    if (tid < GT) s_margin[tid] = p.margin[(int64_t)u * GT + tid];
-    cp_async_wait_all();
-    __syncthreads();
   }
 
-  // ---- quantised scores, kept in registers; histogram of all of them --------
+  // ---- quantised scores of one chunk, kept in registers ----------------------
   const int r = lane % CS;
   int colidx[CS];
 #pragma unroll
@@ -684,52 +509,137 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     colidx[uu] = Q::rb_of(s) * 256 * Q::COLS + Q::col_of(lane, s);
   }
   uint32_t accs[K6_TPT][Q::NACC];
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    if (half == 1) {
-#pragma unroll
-      for (int it = 0; it < HT; ++it) {
-        const int t = t0 + (HT + it) * K6_THREADS + tid;
-        if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
-        else {
-#pragma unroll
-          for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
-        }
-      }
-    }
+  auto load_half = [&](int t0, int half) {
 #pragma unroll
     for (int it = 0; it < HT; ++it) {
-      const int ti = half * HT + it;
-      const int t = t0 + ti * K6_THREADS + tid;
+      const int t = t0 + (half * HT + it) * K6_THREADS + tid;
+      if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
+      else {
 #pragma unroll
-      for (int a = 0; a < Q::NACC; ++a) accs[ti][a] = 0;
-      rotate_bytes<Q::W>(w[it], r);
-#pragma unroll
-      for (int uu = 0; uu < CS; ++uu) {
-        const uint32_t byte = (w[it][uu >> 2] >> (8 * (uu & 3))) & 0xffu;
-        const int e = colidx[uu] + (int)byte * Q::COLS;
-        if constexpr (Q::EW == 4) {
-          accs[ti][0] += reinterpret_cast<const uint32_t*>(qlut)[e];
-        } else if constexpr (Q::EW == 8) {
-          const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
-          accs[ti][0] += x.x; accs[ti][1] += x.y;
-        } else {
-          const uint4 x = reinterpret_cast<const uint4*>(qlut)[e];
-          accs[ti][0] += x.x; accs[ti][1] += x.y; accs[ti][2] += x.z; accs[ti][3] += x.w;
-        }
+        for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
       }
-      if (t >= lo_t && t < hi_t) {
+    }
+  };
+  // scores of chunk c into accs (first half of its codes already in w when
+  // preloaded); with to_hist every in-range score goes to the histograms
+  auto score_chunk = [&](int c, bool preloaded, bool to_hist) {
+    const int t0 = c * K6_CHUNK;
+    const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
+    if (!preloaded) load_half(t0, 0);
 #pragma unroll
-        for (int g = 0; g < GT; ++g) {
-          const int bin = approx_of<GT>(accs[ti], g) >> HSHIFT;
-          atomicAdd(&hist[g * HWORDS + (bin >> 1)], 1u << (16 * (bin & 1)));
+    for (int half = 0; half < 2; ++half) {
+      if (half == 1) load_half(t0, 1);
+#pragma unroll
+      for (int it = 0; it < HT; ++it) {
+        const int ti = half * HT + it;
+        const int t = t0 + ti * K6_THREADS + tid;
+#pragma unroll
+        for (int a = 0; a < Q::NACC; ++a) accs[ti][a] = 0;
+        rotate_bytes<Q::W>(w[it], r);
+#pragma unroll
+        for (int uu = 0; uu < CS; ++uu) {
+          const uint32_t byte = (w[it][uu >> 2] >> (8 * (uu & 3))) & 0xffu;
+          const int e = colidx[uu] + (int)byte * Q::COLS;
+          if constexpr (Q::EW == 4) {
+            accs[ti][0] += reinterpret_cast<const uint32_t*>(qlut)[e];
+          } else if constexpr (Q::EW == 8) {
+            const uint2 x = reinterpret_cast<const uint2*>(qlut)[e];
+            accs[ti][0] += x.x; accs[ti][1] += x.y;
+          } else {
+            const uint4 x = reinterpret_cast<const uint4*>(qlut)[e];
+            accs[ti][0] += x.x; accs[ti][1] += x.y; accs[ti][2] += x.z; accs[ti][3] += x.w;
+          }
+        }
+        if (to_hist && t >= lo_t && t < hi_t) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            const int bin = approx_of<GT>(accs[ti], g) >> HSHIFT;
+            atomicAdd(&hist[g * HWORDS + (bin >> 1)], 1u << (16 * (bin & 1)));
+          }
         }
       }
     }
-  }
+  };
 
-  // ---- threshold: lower edge of the bin holding the k'-th score, less the band
-  if constexpr (FUSED) pool_cluster<GT * HWORDS>(hist, full, R, me); else __syncthreads();
+  // candidates of chunk c from accs: list (token per (head, slot)), exact
+  // rescoring into selection keys, count (-1 when the list overflowed)
+  uint32_t* list = hist;   // [GT][CAND_MAX], the histograms are dead by then
+  static_assert(CAND_MAX <= HWORDS, "candidate list must fit the histogram space");
+  auto emit_chunk = [&](int c) {
+    const int t0 = c * K6_CHUNK;
+    const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
+    {   // per-warp counts first, one atomic per (warp, head), then the slots
+      int wc[GT];
+#pragma unroll
+      for (int g = 0; g < GT; ++g) wc[g] = 0;
+#pragma unroll
+      for (int ti = 0; ti < K6_TPT; ++ti) {
+        const int t = t0 + ti * K6_THREADS + tid;
+        const bool valid = t >= lo_t && t < hi_t;
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+          wc[g] += __popc(__ballot_sync(0xffffffffu, valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g]));
+      }
+      int mine = 0;
+#pragma unroll
+      for (int g = 0; g < GT; ++g) if (lane == g) mine = wc[g];
+      int basev = 0;
+      if (lane < p.G && mine > 0) basev = atomicAdd(&s_cnt[lane], mine);
+#pragma unroll
+      for (int g = 0; g < GT; ++g) wc[g] = __shfl_sync(0xffffffffu, basev, g);   // running slot per head
+#pragma unroll
+      for (int ti = 0; ti < K6_TPT; ++ti) {
+        const int t = t0 + ti * K6_THREADS + tid;
+        const bool valid = t >= lo_t && t < hi_t;
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+          const bool pred = valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g];
+          const unsigned m = __ballot_sync(0xffffffffu, pred);
+          const int slot = wc[g] + __popc(m & ((1u << lane) - 1u));
+          if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)t;
+          wc[g] += __popc(m);
+        }
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int g = 0; g < GT; ++g) { s_nl[g] = acc; acc += (g < p.G) ? min(s_cnt[g], CAND_MAX) : 0; }
+    }
+    __syncthreads();
+    const int n_items = s_nl[GT - 1] + ((GT - 1 < p.G) ? min(s_cnt[GT - 1], CAND_MAX) : 0);
+    uint64_t* keys = p.cand_key + ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
+    const float scale = p.scale;
+    for (int i = tid; i < n_items; i += K6_THREADS) {
+      int g = 0;
+#pragma unroll
+      for (int k = 1; k < GT; ++k) if (i >= s_nl[k]) g = k;
+      const int slot = i - s_nl[g];
+      if (s_cnt[g] > CAND_MAX) continue;   // overflowed: the chunk is rescanned exactly
+      const uint32_t t = list[g * CAND_MAX + slot];
+      uint32_t cw[Q::W];
+      load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
+      const float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
+      float e[CS];
+#pragma unroll
+      for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + s * 256 + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu)) : 0.f;
+      float sum = 0.f;   // reference order: ((0 + T0[c0]) + T1[c1]) + ...
+#pragma unroll
+      for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
+      keys[g * CAND_MAX + slot] = sel_key(fmul(sum, scale), t);
+    }
+    __syncthreads();
+    if (tid < GT) {
+      p.cand_cnt[((int64_t)u * p.n_chunks + c) * GT + tid] =
+          (tid < p.G && s_cnt[tid] > CAND_MAX) ? -1 : (tid < p.G ? s_cnt[tid] : 0);
+      s_cnt[tid] = 0;
+    }
+    __syncthreads();
+  };
+
+  // ---- histograms of every own chunk, pooled; threshold ----------------------
+  for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
+  pool_cluster<GT * HWORDS>(hist, full, R, me);
   if (warp < GT) {
     const int g = warp;
     const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
@@ -738,70 +648,12 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   }
   __syncthreads();
 
-  // ---- candidates: list (token per (head, slot)), then exact rescoring -------
-  uint32_t* list = hist;   // [GT][CAND_MAX], the histograms are dead
-  static_assert(CAND_MAX <= HWORDS, "candidate list must fit the histogram space");
-  {   // per-warp counts first, one atomic per (warp, head), then the slots
-    int wc[GT];
-#pragma unroll
-    for (int g = 0; g < GT; ++g) wc[g] = 0;
-#pragma unroll
-    for (int ti = 0; ti < K6_TPT; ++ti) {
-      const int t = t0 + ti * K6_THREADS + tid;
-      const bool valid = t >= lo_t && t < hi_t;
-#pragma unroll
-      for (int g = 0; g < GT; ++g)
-        wc[g] += __popc(__ballot_sync(0xffffffffu, valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g]));
-    }
-    int mine = 0;
-#pragma unroll
-    for (int g = 0; g < GT; ++g) if (lane == g) mine = wc[g];
-    int basev = 0;
-    if (lane < p.G && mine > 0) basev = atomicAdd(&s_cnt[lane], mine);
-#pragma unroll
-    for (int g = 0; g < GT; ++g) wc[g] = __shfl_sync(0xffffffffu, basev, g);   // running slot per head
-#pragma unroll
-    for (int ti = 0; ti < K6_TPT; ++ti) {
-      const int t = t0 + ti * K6_THREADS + tid;
-      const bool valid = t >= lo_t && t < hi_t;
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        const bool pred = valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g];
-        const unsigned m = __ballot_sync(0xffffffffu, pred);
-        const int slot = wc[g] + __popc(m & ((1u << lane) - 1u));
-        if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)t;
-        wc[g] += __popc(m);
-      }
-    }
+  // ---- candidates: the last scored chunk from registers, the others scored again
+  emit_chunk(me + (n_mine - 1) * R);
+  for (int i = 0; i + 1 < n_mine; ++i) {
+    score_chunk(me + i * R, false, false);
+    emit_chunk(me + i * R);
   }
-  __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int g = 0; g < GT; ++g) { s_nl[g] = acc; acc += (g < p.G) ? min(s_cnt[g], CAND_MAX) : 0; }
-  }
-  __syncthreads();
-  const int n_items = s_nl[GT - 1] + ((GT - 1 < p.G) ? min(s_cnt[GT - 1], CAND_MAX) : 0);
-  uint64_t* keys = p.cand_key + ((int64_t)u * p.n_chunks + c) * GT * CAND_MAX;
-  const float scale = p.scale;
-  for (int i = tid; i < n_items; i += K6_THREADS) {
-    int g = 0;
-#pragma unroll
-    for (int k = 1; k < GT; ++k) if (i >= s_nl[k]) g = k;
-    const int slot = i - s_nl[g];
-    if (s_cnt[g] > CAND_MAX) continue;   // overflowed: the chunk is rescanned exactly
-    const uint32_t t = list[g * CAND_MAX + slot];
-    uint32_t cw[Q::W];
-    load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
-    const float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
-    float e[CS];
-#pragma unroll
-    for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + s * 256 + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu)) : 0.f;
-    float sum = 0.f;   // reference order: ((0 + T0[c0]) + T1[c1]) + ...
-#pragma unroll
-    for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
-    keys[g * CAND_MAX + slot] = sel_key(fmul(sum, scale), t);
-  }
-  if (tid < GT) cnt_out[tid] = (tid < p.G && s_cnt[tid] > CAND_MAX) ? -1 : (tid < p.G ? s_cnt[tid] : 0);
 }
 
 template <int D>

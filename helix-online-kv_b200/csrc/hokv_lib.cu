@@ -98,28 +98,18 @@ static int launch_ex(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st
 
 // Stage 1: K5 (tables, ordinary launch: it reads the queries) then K6
 // (candidates, programmatic launch: it prefetches its codes while K5 runs).
-// Stage 1.  Up to K6_CLUSTER_MAX chunks per unit: one clustered kernel that
-// builds the tables and streams the candidates (ordinary launch: it reads the
-// queries).  Longer contexts: K5 (tables) then K6 (programmatic launch that
-// loads its codes while K5 runs).
+// Stage 1: one thread-block cluster of min(chunks, K6_CLUSTER_MAX) CTAs per
+// unit builds the tables and streams the candidates (ordinary launch: it
+// reads the queries).
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
-  const size_t sm6 = Q::BYTES + (size_t)GT * HWORDS * 4;
-  const dim3 grid6((unsigned)p.n_chunks, (unsigned)(p.B * p.Hkv));
-  if (p.n_chunks <= K6_CLUSTER_MAX) {
-    const size_t smc = sm6 + (size_t)GT * HWORDS * 4;   // pooled histograms
-    if (int e = ensure_smem(k6_candidates<CS, GT, true>, smc)) return e;
-    return launch_ex(k6_candidates<CS, GT, true>, grid6, dim3(K6_THREADS), smc, st, p, "k6_candidates (fused)",
-                     false, p.n_chunks);
-  }
-  const size_t sm5 = (size_t)p.M * stage_rows(p.slots, p.M * p.sd) * p.sd * 4;
-  if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
-  k5_tables<CS, GT><<<dim3((unsigned)(p.B * p.Hkv), (unsigned)GT), K5_THREADS, sm5, st>>>(p);
-  if (int e = check_launch("k5_tables")) return e;
-  if (int e = ensure_smem(k6_candidates<CS, GT, false>, sm6)) return e;
-  return launch_ex(k6_candidates<CS, GT, false>, grid6, dim3(K6_THREADS), sm6, st, p, "k6_candidates", true);
+  const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
+  const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
+  if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
+  return launch_ex(k6_candidates<CS, GT>, dim3((unsigned)R, (unsigned)(p.B * p.Hkv)), dim3(K6_THREADS), sm, st, p,
+                   "k6_candidates", false, R);
 }
 
 static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
