@@ -182,16 +182,15 @@ def test_store_long_context_16k():
     assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "16k") <= 4
 
 
-def test_store_long_context_20k_chunk_thresholds():
-    """20K tokens: 10 candidate chunks per unit, more than one cluster holds,
-    so the tables come from their own kernel and each chunk ranks alone."""
+def test_store_long_context_20k_two_pass_chunks():
+    """20K tokens: 10 chunks over a cluster of 8 CTAs, so two CTAs score two
+    chunks each, once for the histogram and again for the candidate list."""
     st, q, lens = _store(1, 1, 4, 128, 20000, 16, torch.bfloat16, seed=11)
     assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "20k") <= 4
 
 
-def test_store_long_context_64k_streamed_selection():
-    """64K tokens: 32 chunks rank alone, so thousands of candidate keys reach
-    the selection, which then runs as a radix select over the candidate lists."""
+def test_store_long_context_64k():
+    """64K tokens: 32 chunks, four per CTA of the cluster, one unit-wide threshold."""
     st, q, lens = _store(1, 1, 2, 64, 65536, 8, torch.float16, seed=19)
     assert _check_store(st, q, lens, 0.125, 128, 4, 256, "64k") <= 4
 
