@@ -235,14 +235,16 @@ typedef struct hokv_cdc03_args {
 int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes);
 /* Both stages below, in order, on `stream`. */
 int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream);
-/* Stage 1 (gather_pq_scores + the first half of the selection,
- * product_codebook.py:207-227, compressed_attention.py:362-383): stream the
- * PQ codes with 8-bit sub-tables and write, per (sequence, KV head, chunk,
- * query head), the tokens that can still reach the top-k into the workspace. */
+/* Stage 1 (precompute_distance_tables + gather_pq_scores + the first half of
+ * the selection, product_codebook.py:172-227, compressed_attention.py:362-383):
+ * build the sub-tables, stream the PQ codes scored with quantised 16-bit
+ * tables, and write, per (sequence, KV head, chunk, query head), the tokens
+ * that can still reach the top-k with their exact scores (selection keys)
+ * into the workspace. */
 int hokv_cdc03_candidates(const hokv_cdc03_args* a, void* stream);
-/* Stage 2 (compressed_attention.py:384-403): exact fp32 rescoring of the
- * candidates, exact top-k with sinks, softmax attention over the selected
- * cold tokens plus the hot window.  Reads the workspace stage 1 wrote. */
+/* Stage 2 (compressed_attention.py:384-403): exact top-k of the candidate
+ * keys with sinks, softmax attention over the selected cold tokens plus the
+ * hot window.  Reads the workspace stage 1 wrote. */
 int hokv_cdc03_attend(const hokv_cdc03_args* a, void* stream);
 
 /* hokv_cdc03_decode for callers that cannot allocate device memory.  No
