@@ -63,16 +63,19 @@ class CDC03Store:
         """Fit the PQ codebooks of one layer on tokens [0, n_tokens) of every (b, h)
         (ProductCodebook.finalize_calibration, product_codebook.py:86-116)."""
         n = int(n_tokens)
-        data = self.k[layer, :, :, :n, :].float().reshape(self.B * self.H, n, self.D).contiguous()
-        ws = L.workspace(L.lib().hokv_vq_kmeans_workspace_size(n, self.sd, self.M))
-        it = torch.zeros(self.M, dtype=torch.int32, device=data.device)
-        mse = torch.zeros(self.M, dtype=torch.float64, device=data.device)
-        cb = self.codebook[layer].reshape(self.B * self.H, self.M, SLOTS, self.sd)
-        kk = self.cb_k[layer].reshape(self.B * self.H, self.M)
-        for u in range(self.B * self.H):
-            L.check(L.lib().hokv_vq_kmeans(L.ptr(data[u]), n, self.sd, self.D, self.sd, self.M, sub_clusters,
-                                           max_iters, float(rtol), L.ptr(cb[u]), SLOTS, L.ptr(kk[u]), L.ptr(it),
-                                           L.ptr(mse), L.ptr(ws), ws.numel(), L.stream()), "vq_kmeans")
+        U = self.B * self.H
+        # one launch for every (sequence, head, subspace) fit: sets [U * M][n][sd]
+        data = (self.k[layer, :, :, :n, :self.M * self.sd].float().reshape(U, n, self.M, self.sd)
+                .permute(0, 2, 1, 3).contiguous())
+        n_sets = U * self.M
+        ws = L.workspace(L.lib().hokv_vq_kmeans_workspace_size(n, self.sd, n_sets))
+        it = torch.zeros(n_sets, dtype=torch.int32, device=data.device)
+        mse = torch.zeros(n_sets, dtype=torch.float64, device=data.device)
+        cb = self.codebook[layer].reshape(n_sets, SLOTS, self.sd)
+        kk = self.cb_k[layer].reshape(n_sets)
+        L.check(L.lib().hokv_vq_kmeans(L.ptr(data), n, self.sd, self.sd, n * self.sd, n_sets, sub_clusters,
+                                       max_iters, float(rtol), L.ptr(cb), SLOTS, L.ptr(kk), L.ptr(it),
+                                       L.ptr(mse), L.ptr(ws), ws.numel(), L.stream()), "vq_kmeans")
 
     def assign(self, layer: int, start: int, end: int, order: int | None = None):
         """PQ codes of tokens [start, end) of every (b, h) of one layer

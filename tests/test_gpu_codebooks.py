@@ -263,3 +263,23 @@ def test_layer_state_lifecycle():
     mem = ls.memory_bytes()
     assert mem["index_bytes"] == 48 * 2 * dim and mem["total_bytes"] == mem["codebook_bytes"] + mem["index_bytes"]
     assert KVLayerState(0, cfg).memory_bytes()["total_bytes"] == 0
+
+
+def test_store_calibration_matches_product_codebook():
+    """CDC03Store.calibrate fits every (sequence, head, subspace) in one launch;
+    each fit equals ProductCodebook's on the same calibration tokens."""
+    from helix_online_kv.cdc03 import CDC03Store
+    from helix_online_kv.product_codebook import ProductCodebook
+    K, V = O.gen_kv(29, 2, 3, 300, 64)
+    st = CDC03Store(2, 1, 3, 64, 300, n_subspaces=8, dtype=torch.float16)
+    st.k[0, :, :, :300] = torch.from_numpy(K).half().cuda()
+    st.calibrate(0, 128)
+    for b in range(2):
+        for h in range(3):
+            pq = ProductCodebook(n_subspaces=8, sub_clusters=256, head_dim=64)
+            pq.feed_calibration(st.k[0, b, h, :128].float().cpu().numpy())
+            info = pq.finalize_calibration()
+            kk = st.cb_k[0, b, h].cpu().numpy()
+            assert list(kk) == list(info["sub_clusters"])
+            for s, cb in enumerate(pq._codebooks):
+                np.testing.assert_array_equal(st.codebook[0, b, h, s, :kk[s]].cpu().numpy(), cb.centroids)
