@@ -318,9 +318,7 @@ def run_ours(args):
     peak, peak_kind = _peaks()
     k6_gbs = k6_bytes / (k6_ms * 1e-3) / 1e9
     k7_gbs = k7_bytes / (k7_ms * 1e-3) / 1e9
-    fused = (Sc + 2047) // 2048 <= 8   # tables built inside the candidate kernel's clusters
-    s1 = ("k6_candidates (tables fused, thread-block clusters)" if fused else "k5_tables + k6_candidates",
-          k6_gbs, k6_bytes, k6_ms)
+    s1 = ("k6_candidates (tables built in thread-block clusters)", k6_gbs, k6_bytes, k6_ms)
     s2 = ("k7_select_attend", k7_gbs, k7_bytes, k7_ms)
     dom, other = (s1, s2) if k6_ms >= k7_ms else (s2, s1)
 
@@ -403,7 +401,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
         "vq_assign": {"value": as_gbs, "unit": "GB/s", "frac": as_gbs / peak, "vectors": units * n_new,
                       "ms": as_ms, "kernel": "k_pq_assign_seq (fp32 CUDA cores, 4 vectors per thread in registers)"},
-        "gpu_launches": args.steps * Ls * (2 if fused else 3),
+        "gpu_launches": args.steps * Ls * 2,   # k6_candidates + k7_select_attend per layer
         "clocks": clk.summary(),
         "setup_s": t_setup,
     }

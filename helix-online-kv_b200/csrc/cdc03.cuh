@@ -872,13 +872,13 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
         }
         keys[li] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
       }
-      if (tid == 0) s_n = 0;
+      if (tid == 0) s_n = min(n_listed, cr.kp);
       __syncthreads();
-      for (int i = tid; i < n_listed; i += K7_THREADS) {
+      for (int i = tid; i < n_listed; i += K7_THREADS) {   // position = rank: a fixed order
         const uint64_t x = keys[i];
         int rank = 0;
         for (int j = 0; j < n_listed; ++j) rank += keys[j] > x;
-        if (rank < cr.kp) sel[cr.sink + atomicAdd(&s_n, 1)] = (int)key_idx(x);
+        if (rank < cr.kp) sel[cr.sink + rank] = (int)key_idx(x);
       }
     } else {
       // many keys (chunk-local thresholds of long contexts) or overflowed
@@ -1008,9 +1008,17 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
       for_each_key([&](uint64_t key) {
         if (key >= thr) {
           const int slot = atomicAdd(&s_n, 1);
-          if (slot < cr.kp) sel[cr.sink + slot] = (int)key_idx(key);
+          if (slot < K7_CAP) keys[slot] = key;
         }
       });
+      __syncthreads();
+      const int m = min(min(s_n, cr.kp), K7_CAP);
+      for (int i = tid; i < m; i += K7_THREADS) {   // position = rank among the selected: a fixed order
+        const uint64_t x = keys[i];
+        int rank = 0;
+        for (int j = 0; j < m; ++j) rank += keys[j] > x;
+        sel[cr.sink + rank] = (int)key_idx(x);
+      }
     }
     __syncthreads();
     n_sel = cr.sink + min(s_n, cr.kp);

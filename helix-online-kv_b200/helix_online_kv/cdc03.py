@@ -93,6 +93,26 @@ class CDC03Store:
                                            L.ptr(self.cb_k[layer, b]), self.M, L.ptr(out), self.CS,
                                            self.cap * self.CS, self.H, order, L.stream()), "pq_assign")
 
+    # ---- checkpoint / resume ---------------------------------------------------
+    _STATE = ("k", "v", "codes", "codebook", "cb_k", "seq_len")
+
+    def state_dict(self) -> dict:
+        """The store's tensors (exact tiers, codes, codebooks, lengths) and geometry;
+        the reference has no serialization of its codebooks or indices."""
+        state = {name: getattr(self, name) for name in self._STATE}
+        state["geometry"] = dict(batch=self.B, n_layers=self.L, kv_heads=self.H, head_dim=self.D,
+                                 capacity=self.cap, n_subspaces=self.M)
+        return state
+
+    def load_state_dict(self, state: dict) -> None:
+        geo = state["geometry"]
+        mine = dict(batch=self.B, n_layers=self.L, kv_heads=self.H, head_dim=self.D, capacity=self.cap,
+                    n_subspaces=self.M)
+        if geo != mine:
+            raise ValueError(f"Expected shape {mine}, got {geo}")
+        for name in self._STATE:
+            getattr(self, name).copy_(state[name])
+
     # ---- tier aging ----------------------------------------------------------
     def _store_args(self, layer: int) -> L.Cdc03Args:
         a = L.Cdc03Args()

@@ -318,3 +318,20 @@ def test_age_tokens_and_append():
     q = torch.from_numpy(Q).half().cuda()
     _check_store(st, q, [n + 1 for n in lens], 0.125, 128, 4, hot, "after append",
                  exclude_rows={b: {lens[b] - hot} for b in range(B)})
+
+
+def test_store_checkpoint_resume(tmp_path):
+    """state_dict / load_state_dict through torch.save: the restored store
+    decodes bit-identically; a store of another geometry is refused."""
+    from helix_online_kv.cdc03 import CDC03Store
+    st, q, lens = _store(2, 2, 4, 64, 1500, 8, torch.float16, seed=41, seq_lens=[1500, 1100])
+    out1 = st.decode(0, q, 0.125, 64, 4, 128, out_dtype=torch.float32)
+    path = tmp_path / "store.pt"
+    torch.save(st.state_dict(), path)
+    st2 = CDC03Store(2, 1, 2, 64, 1500, n_subspaces=8, dtype=torch.float16)
+    st2.load_state_dict(torch.load(path))
+    out2 = st2.decode(0, q, 0.125, 64, 4, 128, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2)
+    with pytest.raises(ValueError, match="Expected shape"):
+        CDC03Store(2, 1, 2, 64, 1024, n_subspaces=8, dtype=torch.float16).load_state_dict(torch.load(path))
