@@ -663,12 +663,48 @@ struct AttnGeo {
   static constexpr int SUB = 32 / LPT;                   // tokens per warp step
 };
 
+// One lane's slice of a K/V row kept as stored (16-bit values two to a word)
+// and widened to fp32 where it is used: twice the rows in flight per register
+// than fp32 copies.
 template <typename KVT, int DPL>
-__device__ __forceinline__ void load_row(const KVT* p, float (&o)[DPL]) {
+struct RawRow {
+  static constexpr int NW = DPL * (int)sizeof(KVT) / 4;
+  uint32_t w[NW];
+};
+
+template <typename KVT, int DPL>
+__device__ __forceinline__ void load_raw(const KVT* p, RawRow<KVT, DPL>& r) {
+  constexpr int NW = RawRow<KVT, DPL>::NW;
+  static_assert(NW == 2 || NW % 4 == 0, "row slice of 8 or 16k bytes");
+  if constexpr (NW == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    r.w[0] = v.x; r.w[1] = v.y;
+  } else {
 #pragma unroll
-  for (int i = 0; i < DPL; i += 4) {
-    float4 f = load4<KVT>(p + i);
-    o[i] = f.x; o[i + 1] = f.y; o[i + 2] = f.z; o[i + 3] = f.w;
+    for (int i = 0; i < NW / 4; ++i) {
+      const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+      r.w[4 * i] = v.x; r.w[4 * i + 1] = v.y; r.w[4 * i + 2] = v.z; r.w[4 * i + 3] = v.w;
+    }
+  }
+}
+
+template <typename KVT, int DPL>
+__device__ __forceinline__ void unpack_raw(const RawRow<KVT, DPL>& r, float (&o)[DPL]) {
+  if constexpr (std::is_same<KVT, float>::value) {
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[i] = __uint_as_float(r.w[i]);
+  } else if constexpr (std::is_same<KVT, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int i = 0; i < DPL / 2; ++i) {   // bf16 is the top half of an fp32
+      o[2 * i] = __uint_as_float(r.w[i] << 16);
+      o[2 * i + 1] = __uint_as_float(r.w[i] & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < DPL / 2; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.w[i]));
+      o[2 * i] = f.x; o[2 * i + 1] = f.y;
+    }
   }
 }
 
@@ -679,7 +715,7 @@ template <int D, typename KVT>
 struct Attn {
   using A = AttnGeo<D>;
   static constexpr int NW = K7_THREADS / 32;
-  static constexpr int U = 8;
+  static constexpr int U = sizeof(KVT) == 2 ? 16 : 8;   // rows in flight per warp
   float qv[A::DPL];
   float m_run, l_run, acc[A::DPL];
   int sub, sl;
@@ -699,7 +735,8 @@ struct Attn {
   __device__ void run(const KVT* kb, const KVT* vb, int n, int warp, float scale, TokF tok, ScoreF on_score) {
     constexpr int STEP = NW * A::SUB * U;
     for (int ib = warp * A::SUB * U; ib < n; ib += STEP) {
-      float kf[U][A::DPL], vf[U][A::DPL], s[U];
+      RawRow<KVT, A::DPL> kr[U], vr[U];
+      float s[U];
       bool valid[U];
 #pragma unroll
       for (int r = 0; r < U; ++r) {
@@ -707,16 +744,18 @@ struct Attn {
         valid[r] = i < n;
         if (valid[r]) {
           const int t = tok(i);
-          load_row<KVT, A::DPL>(kb + (int64_t)t * D + sl * A::DPL, kf[r]);
-          load_row<KVT, A::DPL>(vb + (int64_t)t * D + sl * A::DPL, vf[r]);
+          load_raw<KVT, A::DPL>(kb + (int64_t)t * D + sl * A::DPL, kr[r]);
+          load_raw<KVT, A::DPL>(vb + (int64_t)t * D + sl * A::DPL, vr[r]);
         }
       }
 #pragma unroll
       for (int r = 0; r < U; ++r) {
         s[r] = 0.f;
         if (valid[r]) {
+          float kf[A::DPL];
+          unpack_raw<KVT, A::DPL>(kr[r], kf);
 #pragma unroll
-          for (int i = 0; i < A::DPL; ++i) s[r] = fmaf(qv[i], kf[r][i], s[r]);
+          for (int i = 0; i < A::DPL; ++i) s[r] = fmaf(qv[i], kf[i], s[r]);
         }
       }
 #pragma unroll
@@ -744,8 +783,10 @@ struct Attn {
           if (valid[r]) {
             const float pe = __expf(s[r] - mn);
             l_run += pe;
+            float vf[A::DPL];
+            unpack_raw<KVT, A::DPL>(vr[r], vf);
 #pragma unroll
-            for (int d = 0; d < A::DPL; ++d) acc[d] = fmaf(pe, vf[r][d], acc[d]);
+            for (int d = 0; d < A::DPL; ++d) acc[d] = fmaf(pe, vf[d], acc[d]);
           }
         }
         m_run = mn;
