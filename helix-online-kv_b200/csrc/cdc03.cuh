@@ -656,9 +656,10 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   }
 }
 
-template <int D>
+template <int D, typename KVT>
 struct AttnGeo {
-  static constexpr int DPL = (D <= 128) ? 4 : D / 32;   // dims per lane
+  // dims per lane: 16 bytes of a row, or D / 32 when that is more
+  static constexpr int DPL = (16 / (int)sizeof(KVT)) > D / 32 ? 16 / (int)sizeof(KVT) : D / 32;
   static constexpr int LPT = D / DPL;                    // lanes per token
   static constexpr int SUB = 32 / LPT;                   // tokens per warp step
 };
@@ -713,9 +714,9 @@ __device__ __forceinline__ void unpack_raw(const RawRow<KVT, DPL>& r, float (&o)
 // ===========================================================================
 template <int D, typename KVT>
 struct Attn {
-  using A = AttnGeo<D>;
+  using A = AttnGeo<D, KVT>;
   static constexpr int NW = K7_THREADS / 32;
-  static constexpr int U = sizeof(KVT) == 2 ? 16 : 8;   // rows in flight per warp
+  static constexpr int U = 8;   // row slices in flight per lane
   float qv[A::DPL];
   float m_run, l_run, acc[A::DPL];
   int sub, sl;
@@ -813,7 +814,7 @@ __host__ __device__ constexpr int k7_stage_bytes() {
 
 template <int D, typename KVT>
 __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
-  using A = AttnGeo<D>;
+  using A = AttnGeo<D, KVT>;
   using AT = Attn<D, KVT>;
   constexpr int NW = AT::NW;
   extern __shared__ __align__(16) unsigned char smem[];
