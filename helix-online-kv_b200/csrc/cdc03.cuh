@@ -797,20 +797,14 @@ struct Attn {
 };
 
 constexpr int K7_RANK_MAX = K7_CAP;   // up to this many keys, selection by rank counting
+constexpr int K7_FAST_SLOTS = 64;     // list slots per chunk read with the counts
+static_assert(8 * K7_FAST_SLOTS <= K7_CAP && K7_FAST_SLOTS <= CAND_MAX && K7_FAST_SLOTS == 64,
+              "fast path: two slots per lane, every chunk's keys fit the key buffer");
 static_assert(K7_THREADS == 256, "k7_select_attend clears a 256-bin histogram with one thread per bin");
 
-// Rows of the K7 staging tile: K and V rows of up to 128 tokens in 64 KB.
-template <int D, typename KVT>
-__host__ __device__ constexpr int k7_stage_rows() {
-  return (65536 / (2 * D * (int)sizeof(KVT))) < 128 ? (65536 / (2 * D * (int)sizeof(KVT))) : 128;
-}
-// Bytes of the staging space: the tile, and at least 64 KB (it also caches the
-// selection keys of long contexts).
-template <int D, typename KVT>
-__host__ __device__ constexpr int k7_stage_bytes() {
-  return 2 * k7_stage_rows<D, KVT>() * D * (int)sizeof(KVT) > 65536 ? 2 * k7_stage_rows<D, KVT>() * D * (int)sizeof(KVT)
-                                                                      : 65536;
-}
+// Shared memory that caches the keys of the radix selection (long contexts),
+// when they fit: 8192 keys.
+constexpr int K7_KEYCACHE_BYTES = 65536;
 
 template <int D, typename KVT>
 __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
@@ -847,31 +841,11 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   AT at;
   at.init(s_q, lane);
 
-  // rows of tokens tok(0..n) staged in shared memory by cp.async, a tile of
-  // k7_stage_rows at a time (one memory round trip per tile), then attended
-  const int stage_rows_n = k7_stage_rows<D, KVT>();
-  KVT* sk = reinterpret_cast<KVT*>(part + NW * (D + 2));
-  KVT* sv = sk + (int64_t)stage_rows_n * D;
-  auto attend_staged = [&](int n_all, auto tok, auto on_score) {
-    constexpr int C16 = D * (int)sizeof(KVT) / 16;
-    for (int base = 0; base < n_all; base += stage_rows_n) {
-      const int n = min(stage_rows_n, n_all - base);
-      for (int i = tid; i < n * 2 * C16; i += K7_THREADS) {
-        const int e = i / (2 * C16), rem = i - e * 2 * C16, kv = rem / C16, ch = rem - kv * C16;
-        const int64_t t = tok(base + e);
-        cp_async16(reinterpret_cast<unsigned char*>(kv == 0 ? sk : sv) + ((int64_t)e * D) * sizeof(KVT) + ch * 16,
-                   reinterpret_cast<const unsigned char*>((kv == 0 ? kb : vb) + t * D) + ch * 16);
-      }
-      cp_async_wait_all();
-      __syncthreads();
-      at.run(sk, sv, n, warp, scale, [&](int i) { return i; }, [&](int i, float s) { on_score(base + i, s); });
-      __syncthreads();
-    }
-  };
+  // key cache of the radix selection (long contexts)
+  uint64_t* kc = reinterpret_cast<uint64_t*>(part + NW * (D + 2));
 
   // ---- hot window: independent of the candidate stage, done before waiting
-  // (rows straight from memory, 8 in flight per warp: the 256 KB of a staged
-  // hot window would cost two tile round trips)
+  // (rows straight from memory, 16 in flight per warp for 16-bit K/V)
   const int n_hot = cr.S - cr.Sc;
   at.run(kb, vb, n_hot, warp, scale, [&](int i) { return cr.Sc + i; }, [](int, float) {});
 
@@ -888,189 +862,223 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     explicit_sel = true;
     const int M = p.M;
     const int64_t cbase_idx = (int64_t)u * p.n_chunks * p.GT;
-    for (int c = tid; c < p.n_chunks; c += K7_THREADS) s_cnt[c] = p.cand_cnt[cbase_idx + (int64_t)c * p.GT + g];
-    __syncthreads();
-    if (tid == 0) {
-      int acc = 0, over = 0;
-      for (int c = 0; c < p.n_chunks; ++c) { s_off[c] = acc; acc += s_cnt[c] > 0 ? s_cnt[c] : 0; over |= s_cnt[c] < 0; }
-      s_off[p.n_chunks] = acc;
-      s_over = over;
+    // common case in one memory round trip: at most NW chunks, none with more
+    // than K7_FAST_SLOTS candidates; warp c loads chunk c's count together with
+    // its first K7_FAST_SLOTS list slots and keeps the slots below the count
+    bool fast = p.n_chunks <= NW;
+    int my_cnt = 0;
+    uint64_t k0 = 0ull, k1 = 0ull;
+    if (fast && warp < p.n_chunks) {
+      const int64_t li = cbase_idx + (int64_t)warp * p.GT + g;
+      my_cnt = __ldcg(p.cand_cnt + li);
+      k0 = __ldcg(p.cand_key + li * CAND_MAX + lane);
+      k1 = __ldcg(p.cand_key + li * CAND_MAX + lane + 32);
+      if (lane == 0) s_cnt[warp] = my_cnt;
     }
-    __syncthreads();
-    if (s_over) {   // exact sub-table of this head, for the rescan of overflowed chunks
-      const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
-      for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
-    }
-    const int n_listed = s_off[p.n_chunks];
-    for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
-    if (!s_over && n_listed <= K7_RANK_MAX) {
-      // few keys: gathered into shared memory; a key is selected when fewer
-      // than k' keys beat it (keys are unique)
-      for (int li = tid; li < n_listed; li += K7_THREADS) {
-        int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
-        while (lo < hi) {
-          const int mid = (lo + hi + 1) >> 1;
-          if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
-        }
-        keys[li] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
+    fast = !__syncthreads_or(!fast || (warp < p.n_chunks && (my_cnt < 0 || my_cnt > K7_FAST_SLOTS)));
+    if (fast) {
+      int off = 0, n_all = 0;
+      for (int c = 0; c < p.n_chunks; ++c) {
+        const int x = s_cnt[c];
+        off += c < warp ? x : 0;
+        n_all += x;
       }
-      if (tid == 0) s_n = min(n_listed, cr.kp);
+      if (warp < p.n_chunks) {
+        if (lane < my_cnt) keys[off + lane] = k0;
+        if (lane + 32 < my_cnt) keys[off + lane + 32] = k1;
+      }
+      for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
+      if (tid == 0) s_n = min(n_all, cr.kp);
       __syncthreads();
-      for (int i = tid; i < n_listed; i += K7_THREADS) {   // position = rank: a fixed order
+      for (int i = tid; i < n_all; i += K7_THREADS) {   // position = rank: a fixed order
         const uint64_t x = keys[i];
         int rank = 0;
-        for (int j = 0; j < n_listed; ++j) rank += keys[j] > x;
+        for (int j = 0; j < n_all; ++j) rank += keys[j] > x;
         if (rank < cr.kp) sel[cr.sink + rank] = (int)key_idx(x);
       }
     } else {
-      // many keys (chunk-local thresholds of long contexts) or overflowed
-      // lists: radix select of the k'-th largest key, 8 bits a round, over the
-      // listed keys and the exact keys of every token of an overflowed chunk
-      // (recomputed each round from the exact sub-table); the selection is
-      // exactly the keys >= that key
-      cp_async_wait_all();
-      const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
-      __shared__ int s_ooff[MAX_CHUNKS], s_nall;   // overflowed chunks: key positions after the listed keys
-      auto for_each_source_key = [&](auto fn) {
-        // listed keys: flat index, 8 loads in flight per thread
-        constexpr int UK = 8;
-        for (int base = tid; base < n_listed; base += UK * K7_THREADS) {
-          uint64_t kk[UK];
-#pragma unroll
-          for (int r = 0; r < UK; ++r) {
-            const int li = base + r * K7_THREADS;
-            kk[r] = 0ull;
-            if (li < n_listed) {
-              int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
-              while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
-              }
-              kk[r] = __ldcg(p.cand_key + (cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo]));
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < UK; ++r)
-            if (base + r * K7_THREADS < n_listed) fn(kk[r], base + r * K7_THREADS);
-        }
-        // overflowed chunks: exact keys of every non-sink token
-        for (int c = 0; c < p.n_chunks; ++c) {
-          if (s_cnt[c] >= 0) {
-            continue;
-          } else {
-            const int clo = max(c * p.chunk, cr.sink), chi = min((c + 1) * p.chunk, cr.Sc);
-            for (int t = clo + tid; t < chi; t += K7_THREADS) {
-              const uint32_t* row = reinterpret_cast<const uint32_t*>(codes + (int64_t)t * p.CS);
-              uint32_t cw[8];
-#pragma unroll
-              for (int w = 0; w < 8; ++w) cw[w] = (w < p.CS / 4) ? __ldg(row + w) : 0u;   // one row, loads in flight together
-              float sum = 0.f;
-              for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[s2 * 256 + ((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu)]);
-              fn(sel_key(fmul(sum, scale), (uint32_t)t), n_listed + s_ooff[c] + (t - clo));
-            }
-          }
-        }
-      };
-      // every key once into the (idle) row staging space when they fit there
+      for (int c = tid; c < p.n_chunks; c += K7_THREADS) s_cnt[c] = p.cand_cnt[cbase_idx + (int64_t)c * p.GT + g];
+      __syncthreads();
       if (tid == 0) {
-        int acc = 0;
-        for (int c = 0; c < p.n_chunks; ++c) {
-          s_ooff[c] = acc;
-          if (s_cnt[c] < 0) acc += max(0, min((c + 1) * p.chunk, cr.Sc) - max(c * p.chunk, cr.sink));
-        }
-        s_nall = n_listed + acc;
+        int acc = 0, over = 0;
+        for (int c = 0; c < p.n_chunks; ++c) { s_off[c] = acc; acc += s_cnt[c] > 0 ? s_cnt[c] : 0; over |= s_cnt[c] < 0; }
+        s_off[p.n_chunks] = acc;
+        s_over = over;
       }
       __syncthreads();
-      uint64_t* kc = reinterpret_cast<uint64_t*>(sk);
-      const int kc_cap = k7_stage_bytes<D, KVT>() / 8;
-      const bool cached = s_nall <= kc_cap;
-      if (cached) {
-        for_each_source_key([&](uint64_t key, int pos) { kc[pos] = key; });
-        __syncthreads();
+      if (s_over) {   // exact sub-table of this head, for the rescan of overflowed chunks
+        const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
+        for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
       }
-      auto for_each_key = [&](auto fn) {
+      const int n_listed = s_off[p.n_chunks];
+      for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
+      if (!s_over && n_listed <= K7_RANK_MAX) {
+        // few keys: gathered into shared memory; a key is selected when fewer
+        // than k' keys beat it (keys are unique)
+        for (int li = tid; li < n_listed; li += K7_THREADS) {
+          int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
+          }
+          keys[li] = p.cand_key[(cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo])];
+        }
+        if (tid == 0) s_n = min(n_listed, cr.kp);
+        __syncthreads();
+        for (int i = tid; i < n_listed; i += K7_THREADS) {   // position = rank: a fixed order
+          const uint64_t x = keys[i];
+          int rank = 0;
+          for (int j = 0; j < n_listed; ++j) rank += keys[j] > x;
+          if (rank < cr.kp) sel[cr.sink + rank] = (int)key_idx(x);
+        }
+      } else {
+        // many keys (chunk-local thresholds of long contexts) or overflowed
+        // lists: radix select of the k'-th largest key, 8 bits a round, over the
+        // listed keys and the exact keys of every token of an overflowed chunk
+        // (recomputed each round from the exact sub-table); the selection is
+        // exactly the keys >= that key
+        cp_async_wait_all();
+        const uint8_t* codes = p.codes + (int64_t)b * p.c_sb + (int64_t)h * p.c_sh;
+        __shared__ int s_ooff[MAX_CHUNKS], s_nall;   // overflowed chunks: key positions after the listed keys
+        auto for_each_source_key = [&](auto fn) {
+          // listed keys: flat index, 8 loads in flight per thread
+          constexpr int UK = 8;
+          for (int base = tid; base < n_listed; base += UK * K7_THREADS) {
+            uint64_t kk[UK];
+  #pragma unroll
+            for (int r = 0; r < UK; ++r) {
+              const int li = base + r * K7_THREADS;
+              kk[r] = 0ull;
+              if (li < n_listed) {
+                int lo = 0, hi = p.n_chunks - 1;   // chunk c with s_off[c] <= li < s_off[c + 1]
+                while (lo < hi) {
+                  const int mid = (lo + hi + 1) >> 1;
+                  if (s_off[mid] <= li) lo = mid; else hi = mid - 1;
+                }
+                kk[r] = __ldcg(p.cand_key + (cbase_idx + (int64_t)lo * p.GT + g) * CAND_MAX + (li - s_off[lo]));
+              }
+            }
+  #pragma unroll
+            for (int r = 0; r < UK; ++r)
+              if (base + r * K7_THREADS < n_listed) fn(kk[r], base + r * K7_THREADS);
+          }
+          // overflowed chunks: exact keys of every non-sink token
+          for (int c = 0; c < p.n_chunks; ++c) {
+            if (s_cnt[c] >= 0) {
+              continue;
+            } else {
+              const int clo = max(c * p.chunk, cr.sink), chi = min((c + 1) * p.chunk, cr.Sc);
+              for (int t = clo + tid; t < chi; t += K7_THREADS) {
+                const uint32_t* row = reinterpret_cast<const uint32_t*>(codes + (int64_t)t * p.CS);
+                uint32_t cw[8];
+  #pragma unroll
+                for (int w = 0; w < 8; ++w) cw[w] = (w < p.CS / 4) ? __ldg(row + w) : 0u;   // one row, loads in flight together
+                float sum = 0.f;
+                for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[s2 * 256 + ((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu)]);
+                fn(sel_key(fmul(sum, scale), (uint32_t)t), n_listed + s_ooff[c] + (t - clo));
+              }
+            }
+          }
+        };
+        // every key once into the (idle) row staging space when they fit there
+        if (tid == 0) {
+          int acc = 0;
+          for (int c = 0; c < p.n_chunks; ++c) {
+            s_ooff[c] = acc;
+            if (s_cnt[c] < 0) acc += max(0, min((c + 1) * p.chunk, cr.Sc) - max(c * p.chunk, cr.sink));
+          }
+          s_nall = n_listed + acc;
+        }
+        __syncthreads();
+          const int kc_cap = K7_KEYCACHE_BYTES / 8;
+        const bool cached = s_nall <= kc_cap;
         if (cached) {
-          for (int i = tid; i < s_nall; i += K7_THREADS) fn(kc[i]);
-        } else {
-          for_each_source_key([&](uint64_t key, int) { fn(key); });
+          for_each_source_key([&](uint64_t key, int pos) { kc[pos] = key; });
+          __syncthreads();
         }
-      };
-      __shared__ unsigned long long s_pre, s_msk;
-      __shared__ int s_need, s_done;
-      if (tid == 0) { s_pre = 0ull; s_msk = 0ull; s_need = cr.kp; s_done = 0; }
-      __syncthreads();
-      for (int shift = 56; shift >= 0; shift -= 8) {
-        if (s_done) break;   // uniform: read after a barrier
-        hist[tid] = 0;       // K7_THREADS == 256 bins
+        auto for_each_key = [&](auto fn) {
+          if (cached) {
+            for (int i = tid; i < s_nall; i += K7_THREADS) fn(kc[i]);
+          } else {
+            for_each_source_key([&](uint64_t key, int) { fn(key); });
+          }
+        };
+        __shared__ unsigned long long s_pre, s_msk;
+        __shared__ int s_need, s_done;
+        if (tid == 0) { s_pre = 0ull; s_msk = 0ull; s_need = cr.kp; s_done = 0; }
         __syncthreads();
-        const unsigned long long pre = s_pre, msk = s_msk;
+        for (int shift = 56; shift >= 0; shift -= 8) {
+          if (s_done) break;   // uniform: read after a barrier
+          hist[tid] = 0;       // K7_THREADS == 256 bins
+          __syncthreads();
+          const unsigned long long pre = s_pre, msk = s_msk;
+          for_each_key([&](uint64_t key) {
+            if ((key & msk) == pre) atomicAdd(&hist[(int)((key >> shift) & 255u)], 1u);
+          });
+          __syncthreads();
+          if (warp == 0) {
+            const int need = s_need;
+            uint32_t ls = 0;
+  #pragma unroll
+            for (int i = 0; i < 8; ++i) ls += hist[lane * 8 + i];
+            uint32_t suf = ls;
+  #pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
+              if (lane + o < 32) suf += t;
+            }
+            const unsigned ball = __ballot_sync(0xffffffffu, suf >= (uint32_t)need);
+            if (ball == 0u) {
+              if (lane == 0) s_done = 1;   // fewer matching keys than needed: take them all
+            } else {
+              const int lstar = 31 - __clz((int)ball);
+              if (lane == lstar) {
+                uint32_t cum = suf - ls;
+                for (int i = 7; i >= 0; --i) {
+                  const int d = lane * 8 + i;
+                  const uint32_t hd = hist[d];
+                  if (cum + hd >= (uint32_t)need) {
+                    const int rest = need - (int)cum;
+                    s_pre = pre | ((unsigned long long)d << shift);
+                    s_msk = msk | (255ull << shift);
+                    s_need = rest;
+                    if ((int)hd == rest || shift == 0) s_done = 1;
+                    break;
+                  }
+                  cum += hd;
+                }
+              }
+            }
+          }
+          __syncthreads();
+        }
+        if (tid == 0) s_n = 0;
+        __syncthreads();
+        const unsigned long long thr = s_pre;
         for_each_key([&](uint64_t key) {
-          if ((key & msk) == pre) atomicAdd(&hist[(int)((key >> shift) & 255u)], 1u);
+          if (key >= thr) {
+            const int slot = atomicAdd(&s_n, 1);
+            if (slot < K7_CAP) keys[slot] = key;
+          }
         });
         __syncthreads();
-        if (warp == 0) {
-          const int need = s_need;
-          uint32_t ls = 0;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) ls += hist[lane * 8 + i];
-          uint32_t suf = ls;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
-            if (lane + o < 32) suf += t;
-          }
-          const unsigned ball = __ballot_sync(0xffffffffu, suf >= (uint32_t)need);
-          if (ball == 0u) {
-            if (lane == 0) s_done = 1;   // fewer matching keys than needed: take them all
-          } else {
-            const int lstar = 31 - __clz((int)ball);
-            if (lane == lstar) {
-              uint32_t cum = suf - ls;
-              for (int i = 7; i >= 0; --i) {
-                const int d = lane * 8 + i;
-                const uint32_t hd = hist[d];
-                if (cum + hd >= (uint32_t)need) {
-                  const int rest = need - (int)cum;
-                  s_pre = pre | ((unsigned long long)d << shift);
-                  s_msk = msk | (255ull << shift);
-                  s_need = rest;
-                  if ((int)hd == rest || shift == 0) s_done = 1;
-                  break;
-                }
-                cum += hd;
-              }
-            }
-          }
+        const int m = min(min(s_n, cr.kp), K7_CAP);
+        for (int i = tid; i < m; i += K7_THREADS) {   // position = rank among the selected: a fixed order
+          const uint64_t x = keys[i];
+          int rank = 0;
+          for (int j = 0; j < m; ++j) rank += keys[j] > x;
+          sel[cr.sink + rank] = (int)key_idx(x);
         }
-        __syncthreads();
       }
-      if (tid == 0) s_n = 0;
-      __syncthreads();
-      const unsigned long long thr = s_pre;
-      for_each_key([&](uint64_t key) {
-        if (key >= thr) {
-          const int slot = atomicAdd(&s_n, 1);
-          if (slot < K7_CAP) keys[slot] = key;
-        }
-      });
-      __syncthreads();
-      const int m = min(min(s_n, cr.kp), K7_CAP);
-      for (int i = tid; i < m; i += K7_THREADS) {   // position = rank among the selected: a fixed order
-        const uint64_t x = keys[i];
-        int rank = 0;
-        for (int j = 0; j < m; ++j) rank += keys[j] > x;
-        sel[cr.sink + rank] = (int)key_idx(x);
-      }
-    }
+    }   // general path
     __syncthreads();
     n_sel = cr.sink + min(s_n, cr.kp);
     __syncthreads();
   }
 
-  // ---- exact attention over the selected cold tokens: rows staged in shared
-  // memory by cp.async, a tile of K7_STAGE rows at a time (one memory round
-  // trip per tile instead of one per batch of rows)
-  attend_staged(n_sel, [&](int i) { return (int64_t)(explicit_sel ? sel[i] : i); }, [&](int i, float s) {
+  // ---- exact attention over the selected cold tokens, rows straight from
+  // memory (16 rows in flight per warp: one round trip for 128 rows)
+  at.run(kb, vb, n_sel, warp, scale, [&](int i) { return explicit_sel ? sel[i] : i; }, [&](int i, float s) {
     if (want_scores && at.sl == 0 && i < sel_cap) p.sel_score[sel_base + i] = s;
   });
 

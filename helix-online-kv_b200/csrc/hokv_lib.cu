@@ -133,7 +133,7 @@ static int qimg_bytes_for(int CS, int GT) {
 template <int D, typename KVT>
 static int launch_k7(const Cdc03P& p, cudaStream_t st) {
   const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
-                    (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)k7_stage_bytes<D, KVT>();
+                    (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)K7_KEYCACHE_BYTES;
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
   return launch_ex(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
                    "k7_select_attend", true);
