@@ -195,6 +195,15 @@ def test_store_long_context_64k():
     assert _check_store(st, q, lens, 0.125, 128, 4, 256, "64k") <= 4
 
 
+@pytest.mark.parametrize("top_k", [300, 600])
+def test_store_16k_list_sizes(top_k):
+    """16K tokens, 8 chunks: top-300 leaves 33 to 64 candidates per chunk (the
+    attention stage reads each chunk's count with its first 64 keys, two per
+    lane); top-600 leaves more than 64 (counts first, then the keys)."""
+    st, q, lens = _store(1, 1, 2, 64, 16384, 8, torch.float16, seed=23)
+    assert _check_store(st, q, lens, 0.125, top_k, 4, 256, f"16k top{top_k}") <= 4
+
+
 def test_store_group_of_three_uneven_cluster():
     """G = 3 query heads per KV head (one padded score lane) and 3 chunks per
     unit, so the cluster splits 4 subspace groups unevenly over 3 CTAs."""
