@@ -26,6 +26,7 @@
 namespace hokv {
 
 constexpr int K6_THREADS = 256;
+constexpr int K6_FIRST_ROWS = 128;  // codebook rows per subspace staged before the live counts are read
 
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
@@ -402,12 +403,20 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     const int s_begin = grp0 * GS, s_end = min(grp1 * GS, M);
     const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
     // own codebook rows into shared memory (the image space is free until the
-    // image is loaded), with the queries
-    const int64_t blk = (int64_t)max(0, s_end - s_begin) * p.slots * p.sd;   // floats
+    // image is loaded), with the queries: the first K6_FIRST_ROWS rows of each
+    // subspace now, the live rows past them (if any) once the counts are known
+    const int64_t per_s = (int64_t)p.slots * p.sd;                           // floats per subspace
+    const int64_t blk = (int64_t)max(0, s_end - s_begin) * per_s;
     const bool staged = blk * 4 <= Q::BYTES;
+    const float* src = cbase + (int64_t)s_begin * per_s;
+    const int first = min(p.slots, K6_FIRST_ROWS);
+    const int row16 = p.sd / 4;                                              // 16-byte pieces per row
     if (staged) {
-      const float* src = cbase + (int64_t)s_begin * p.slots * p.sd;
-      for (int64_t i = tid; i < blk / 4; i += K6_THREADS) cp_async16(qlut + i * 16, src + i * 4);
+      const int64_t n16 = (int64_t)(s_end - s_begin) * first * row16;
+      for (int64_t i = tid; i < n16; i += K6_THREADS) {
+        const int64_t sr = i / (first * row16), off = sr * per_s + (i - sr * first * row16) * 4;
+        cp_async16(qlut + off * 4, src + off);
+      }
     }
     float* sq = reinterpret_cast<float*>(hist);   // [GT][D], dead before the histograms
     for (int i = tid; i < GT * p.D; i += K6_THREADS) {
@@ -421,6 +430,19 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
     cp_async_wait_all();
     __syncthreads();
+    if (staged && p.slots > first) {
+      bool more = false;   // the same in every thread: the counts are in shared memory
+      for (int sx = s_begin; sx < s_end; ++sx) more |= s_k[sx] > first;
+      if (more) {
+        for (int sx = s_begin; sx < s_end; ++sx) {
+          const int64_t base = (int64_t)(sx - s_begin) * per_s + (int64_t)first * p.sd;
+          const int64_t n16 = (int64_t)max(0, s_k[sx] - first) * row16;
+          for (int64_t i = tid; i < n16; i += K6_THREADS) cp_async16(qlut + (base + i * 4) * 4, src + base + i * 4);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+      }
+    }
     float tv[2][GT];
     const float* rows = staged ? reinterpret_cast<const float*>(qlut) : cbase;
     const int s_off = staged ? s_begin : 0;

@@ -204,6 +204,15 @@ def test_store_16k_list_sizes(top_k):
     assert _check_store(st, q, lens, 0.125, top_k, 4, 256, f"16k top{top_k}") <= 4
 
 
+def test_store_more_than_128_live_centroids():
+    """Codebooks calibrated on 300 tokens keep up to 256 live centroids per
+    subspace: the candidate stage reads the rows past the first 128 in a
+    second copy, once it has the live counts."""
+    st, q, lens = _store(1, 2, 4, 128, 5000, 16, torch.bfloat16, seed=29, cal=300)
+    assert int(st.cb_k[0].max()) > 128
+    assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "cal300") <= 4
+
+
 def test_store_group_of_three_uneven_cluster():
     """G = 3 query heads per KV head (one padded score lane) and 3 chunks per
     unit, so the cluster splits 4 subspace groups unevenly over 3 CTAs."""
