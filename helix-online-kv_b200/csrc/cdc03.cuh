@@ -820,7 +820,7 @@ struct Attn {
 
 constexpr int K7_RANK_MAX = K7_CAP;   // up to this many keys, selection by rank counting
 constexpr int K7_FAST_SLOTS = 64;     // list slots per chunk read with the counts
-static_assert(8 * K7_FAST_SLOTS <= K7_CAP && K7_FAST_SLOTS <= CAND_MAX && K7_FAST_SLOTS == 64,
+static_assert(8 * K7_FAST_SLOTS + 4 <= K7_CAP && K7_FAST_SLOTS <= CAND_MAX && K7_FAST_SLOTS == 64,
               "fast path: two slots per lane, every chunk's keys fit the key buffer");
 static_assert(K7_THREADS == 256, "k7_select_attend clears a 256-bin histogram with one thread per bin");
 
@@ -910,12 +910,19 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
         if (lane + 32 < my_cnt) keys[off + lane + 32] = k1;
       }
       for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
+      if (tid < 4) keys[n_all + tid] = 0ull;   // padding to a multiple of 4: a zero key beats none
       if (tid == 0) s_n = min(n_all, cr.kp);
       __syncthreads();
+      const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(keys);
+      const int n4 = (n_all + 3) >> 2;
       for (int i = tid; i < n_all; i += K7_THREADS) {   // position = rank: a fixed order
         const uint64_t x = keys[i];
         int rank = 0;
-        for (int j = 0; j < n_all; ++j) rank += keys[j] > x;
+#pragma unroll 4
+        for (int j = 0; j < n4; ++j) {
+          const ulonglong2 a = k2[2 * j], c = k2[2 * j + 1];
+          rank += (int)(a.x > x) + (int)(a.y > x) + (int)(c.x > x) + (int)(c.y > x);
+        }
         if (rank < cr.kp) sel[cr.sink + rank] = (int)key_idx(x);
       }
     } else {
