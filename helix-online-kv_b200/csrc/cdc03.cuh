@@ -21,6 +21,7 @@
 #pragma once
 #include "hokv_common.cuh"
 #include <cooperative_groups.h>
+#include <climits>
 #include <type_traits>
 
 namespace hokv {
@@ -590,37 +591,45 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   auto emit_chunk = [&](int c) {
     const int t0 = c * K6_CHUNK;
     const int lo_t = max(t0, cr.sink), hi_t = min(t0 + K6_CHUNK, cr.Sc);
-    {   // per-warp counts first, one atomic per (warp, head), then the slots
-      int wc[GT];
+    {   // candidates as one bit per (token, head) of this thread; the warp
+        // visits only the bits some lane has set, twice: per-warp counts (one
+        // atomic per (warp, head)), then the slots, in (token, head) order
+      using MT = typename std::conditional<(K6_TPT * GT <= 32), uint32_t, unsigned long long>::type;
+      MT mask = 0;
+      int thr[GT];
 #pragma unroll
-      for (int g = 0; g < GT; ++g) wc[g] = 0;
+      for (int g = 0; g < GT; ++g) thr[g] = g < p.G ? s_thr[g] : INT_MAX;   // padded heads list nothing
 #pragma unroll
       for (int ti = 0; ti < K6_TPT; ++ti) {
         const int t = t0 + ti * K6_THREADS + tid;
         const bool valid = t >= lo_t && t < hi_t;
 #pragma unroll
         for (int g = 0; g < GT; ++g)
-          wc[g] += __popc(__ballot_sync(0xffffffffu, valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g]));
+          if (valid && approx_of<GT>(accs[ti], g) >= thr[g]) mask |= (MT)1 << (ti * GT + g);
       }
-      int mine = 0;
-#pragma unroll
-      for (int g = 0; g < GT; ++g) if (lane == g) mine = wc[g];
-      int basev = 0;
-      if (lane < p.G && mine > 0) basev = atomicAdd(&s_cnt[lane], mine);
-#pragma unroll
-      for (int g = 0; g < GT; ++g) wc[g] = __shfl_sync(0xffffffffu, basev, g);   // running slot per head
-#pragma unroll
-      for (int ti = 0; ti < K6_TPT; ++ti) {
-        const int t = t0 + ti * K6_THREADS + tid;
-        const bool valid = t >= lo_t && t < hi_t;
-#pragma unroll
-        for (int g = 0; g < GT; ++g) {
-          const bool pred = valid && g < p.G && approx_of<GT>(accs[ti], g) >= s_thr[g];
-          const unsigned m = __ballot_sync(0xffffffffu, pred);
-          const int slot = wc[g] + __popc(m & ((1u << lane) - 1u));
-          if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)t;
-          wc[g] += __popc(m);
-        }
+      MT um;
+      if constexpr (sizeof(MT) == 4) {
+        um = __reduce_or_sync(0xffffffffu, mask);
+      } else {
+        um = ((MT)__reduce_or_sync(0xffffffffu, (unsigned)(mask >> 32)) << 32) |
+             (MT)__reduce_or_sync(0xffffffffu, (unsigned)mask);
+      }
+      auto low_bit = [](MT x) { return sizeof(MT) == 4 ? __ffs((unsigned)x) - 1 : __ffsll((long long)x) - 1; };
+      int mine = 0;   // lane g: this warp's candidates of head g
+      for (MT r = um; r; r &= r - 1) {
+        const int bit = low_bit(r);
+        const unsigned m = __ballot_sync(0xffffffffu, (unsigned)(mask >> bit) & 1u);
+        if (lane == (bit & (GT - 1))) mine += __popc(m);
+      }
+      int run = 0;    // lane g: next slot of head g
+      if (lane < p.G && mine > 0) run = atomicAdd(&s_cnt[lane], mine);
+      for (MT r = um; r; r &= r - 1) {
+        const int bit = low_bit(r), g = bit & (GT - 1), ti = bit / GT;
+        const bool pred = (unsigned)(mask >> bit) & 1u;
+        const unsigned m = __ballot_sync(0xffffffffu, pred);
+        const int slot = __shfl_sync(0xffffffffu, run, g) + __popc(m & ((1u << lane) - 1u));
+        if (pred && slot < CAND_MAX) list[g * CAND_MAX + slot] = (uint32_t)(t0 + ti * K6_THREADS + tid);
+        if (lane == g) run += __popc(m);
       }
     }
     __syncthreads();
