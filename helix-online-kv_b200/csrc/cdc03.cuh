@@ -392,12 +392,6 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
     __shared__ int s_k[32];
     cluster_arrive_relaxed();   // phase A: this CTA runs
-    for (int i = 0; i < n_mine; ++i) {   // this CTA's codes into L2 while the tables are built
-      const int t0 = (me + i * R) * K6_CHUNK;
-      const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
-      for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
-    }
     constexpr int GS = 16 / Q::EW;                 // subspaces per 16-byte group
     const int ngm = (M + GS - 1) / GS;             // groups holding real subspaces
     const int grp0 = me * ngm / R, grp1 = (me + 1) * ngm / R;
@@ -453,6 +447,14 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       case 16: lut_dots<GT, 16>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
       case 32: lut_dots<GT, 32>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
       default: dev_flag(HOKV_ERR_DEVICE_INPUT);
+    }
+    // this CTA's codes into L2 while the cluster exchanges and quantises the
+    // tables (issued after the table reads, which are on the critical path)
+    for (int i = 0; i < n_mine; ++i) {
+      const int t0 = (me + i * R) * K6_CHUNK;
+      const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
+      for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
     }
     __syncthreads();
     cluster_wait();             // phase A: every CTA of the cluster runs
