@@ -576,10 +576,20 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
           }
         }
         if (to_hist && t >= lo_t && t < hi_t) {
+          if constexpr (GT == 1) {
+            const int bin = approx_of<GT>(accs[ti], 0) >> HSHIFT;
+            atomicAdd(&hist[bin >> 1], 1u << (16 * (bin & 1)));
+          } else {
+            // straight from the packed lanes: the bin of a 16-bit score v is
+            // v >> 6, its word v >> 7, its half bit 6 of v
+            static_assert(HSHIFT == 6 && HWORDS == 512, "bin arithmetic below");
 #pragma unroll
-          for (int g = 0; g < GT; ++g) {
-            const int bin = approx_of<GT>(accs[ti], g) >> HSHIFT;
-            atomicAdd(&hist[g * HWORDS + (bin >> 1)], 1u << (16 * (bin & 1)));
+            for (int a = 0; a < Q::NACC; ++a) {
+              const uint32_t x = accs[ti][a];
+              const int gl = (GT == 2) ? 0 : (a >> 1) * 4 + (a & 1), gh = (GT == 2) ? 1 : gl + 2;
+              atomicAdd(&hist[gl * HWORDS + ((x >> 7) & (HWORDS - 1))], 1u << ((x >> 2) & 16u));
+              atomicAdd(&hist[gh * HWORDS + (x >> 23)], 1u << ((x >> 18) & 16u));
+            }
           }
         }
       }
