@@ -213,6 +213,19 @@ def test_store_more_than_128_live_centroids():
     assert _check_store(st, q, lens, 1 / np.sqrt(128), 128, 4, 256, "cal300") <= 4
 
 
+@pytest.mark.parametrize("D,M,dtype", [
+    (256, 16, torch.float16),    # 8 dims per lane, a whole warp per row
+    (32, 8, torch.bfloat16),     # 8 dims per lane, 4 lanes per row, 8 rows per warp step
+    (128, 16, torch.float32),    # fp32 K/V: 4 dims (16 bytes) per lane
+    (256, 32, torch.float32),    # fp32 K/V, 32-byte row slices, 32-byte code rows
+])
+def test_store_head_dims_and_kv_dtypes(D, M, dtype):
+    """Head dims 32 and 256 and fp32 K/V stores: the attention loop's per-lane
+    row slices and the code widths that the 16K workload does not reach."""
+    st, q, lens = _store(1, 2, 4, D, 3000, M, dtype, seed=D + M, seq_lens=[2900])
+    assert _check_store(st, q, lens, 1 / np.sqrt(D), 128, 4, 256, f"D{D} M{M} {dtype}") <= 4
+
+
 def test_store_group_of_three_uneven_cluster():
     """G = 3 query heads per KV head (one padded score lane) and 3 chunks per
     unit, so the cluster splits 4 subspace groups unevenly over 3 CTAs."""
