@@ -256,13 +256,18 @@ __device__ __forceinline__ void pool_cluster(const uint32_t* hist, uint32_t* ful
 // the histogram holds fewer than kp items.  One warp; lane L owns bins
 // [32L, 32L + 32).
 __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane) {
+  static_assert(HWORDS == 512, "32 lanes x 16 words");
+  // lane L's 16 words as four 16-byte loads, rotated by lane so that a quarter
+  // warp spreads over the bank groups
+  const uint4* h4 = reinterpret_cast<const uint4*>(h);
   uint32_t ls = 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint32_t w = h[lane * 16 + i];
-    ls += (w & 0xffffu) + (w >> 16);
+  for (int k = 0; k < 4; ++k) {
+    const uint4 v = h4[lane * 4 + ((k + lane) & 3)];
+    ls += (v.x & 0xffffu) + (v.x >> 16) + (v.y & 0xffffu) + (v.y >> 16) + (v.z & 0xffffu) + (v.z >> 16) +
+          (v.w & 0xffffu) + (v.w >> 16);
   }
-  uint32_t suf = ls;
+  uint32_t suf = ls;   // items in lanes >= this one's bins
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t t = __shfl_down_sync(0xffffffffu, suf, o);
@@ -271,18 +276,19 @@ __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane)
   const unsigned ball = __ballot_sync(0xffffffffu, suf >= kp);
   if (ball == 0u) return -1;
   const int lstar = 31 - __clz((int)ball);
-  int bs = -1;
-  if (lane == lstar) {
-    uint32_t cum = suf - ls;
-    for (int i = 15; i >= 0 && bs < 0; --i) {
-      const uint32_t w = h[lane * 16 + i];
-      cum += w >> 16;
-      if (cum >= kp) { bs = lane * 32 + 2 * i + 1; break; }
-      cum += w & 0xffffu;
-      if (cum >= kp) bs = lane * 32 + 2 * i;
-    }
+  // inside lane lstar's 32 bins: lane j takes bin 32 * lstar + j (bin 2i is the
+  // low half of word i), and the warp finds the highest j whose suffix count,
+  // with the items above the range, still reaches kp
+  const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
+  const uint32_t w = h[lstar * 16 + (lane >> 1)];
+  uint32_t c = (lane & 1) ? (w >> 16) : (w & 0xffffu);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_down_sync(0xffffffffu, c, o);
+    if (lane + o < 32) c += t;
   }
-  return __shfl_sync(0xffffffffu, bs, lstar);
+  const unsigned b2 = __ballot_sync(0xffffffffu, above + c >= kp);
+  return lstar * 32 + (31 - __clz((int)b2));
 }
 
 // Resident CTAs per SM: 4 (64 registers) unless the score lanes need more.
