@@ -33,7 +33,10 @@ constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
 constexpr int K7_CAP = 1024;         // key buffer of the exact selection (rank counting)
 constexpr int TOPK_MAX = 1024;       // largest top_k with k < S_c
-constexpr int MAX_CHUNKS = 512;      // K6 chunks per (sequence, KV head)
+// K6 chunks per (sequence, KV head): a CTA then scores at most 31 chunks, so
+// none of its 16-bit histogram counters can exceed 31 x 2048 = 63,488
+// (507,904 cold tokens per sequence)
+constexpr int MAX_CHUNKS = 248;
 
 struct Cdc03P {
   int B, Hkv, G, D, M, sd, CS, slots, top_k, sink, hot;
@@ -235,14 +238,22 @@ __device__ __forceinline__ void pool_cluster(const uint32_t* hist, uint32_t* ful
   for (int i = threadIdx.x; i < per; i += blockDim.x) {
     const int v = me * per + i;
     if (v >= NV) break;
-    uint4 acc = make_uint4(0u, 0u, 0u, 0u);
+    // each 16-bit counter summed in 32 bits and saturated at 65535: an
+    // undercount only lowers the threshold (more candidates, same selection)
+    uint32_t lo[4] = {0u, 0u, 0u, 0u}, hi[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk) {
       if (rk < R) {
         const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(const_cast<uint32_t*>(hist), (unsigned)rk))[v];
-        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { lo[k] += xs[k] & 0xffffu; hi[k] += xs[k] >> 16; }
       }
     }
+    uint32_t ws[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ws[k] = min(lo[k], 0xffffu) | (min(hi[k], 0xffffu) << 16);
+    const uint4 acc = make_uint4(ws[0], ws[1], ws[2], ws[3]);
 #pragma unroll
     for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk)
       if (rk < R) reinterpret_cast<uint4*>(cl.map_shared_rank(full, (unsigned)rk))[v] = acc;
@@ -589,6 +600,8 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
             // straight from the packed lanes: the bin of a 16-bit score v is
             // v >> 6, its word v >> 7, its half bit 6 of v
             static_assert(HSHIFT == 6 && HWORDS == 512, "bin arithmetic below");
+            static_assert((MAX_CHUNKS + K6_CLUSTER_MAX - 1) / K6_CLUSTER_MAX * K6_CHUNK <= 65535,
+                          "a CTA's 16-bit bin counters cannot overflow");
 #pragma unroll
             for (int a = 0; a < Q::NACC; ++a) {
               const uint32_t x = accs[ti][a];

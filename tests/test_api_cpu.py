@@ -127,3 +127,26 @@ def test_no_cpu_fallback():
                            0.3)
     from helix_online_kv.triton_attention import _HAS_TRITON
     assert _HAS_TRITON is False
+
+
+def test_cdc03_context_limit_is_refused():
+    """Contexts needing more than 248 candidate chunks of 2048 tokens per
+    (sequence, KV head) are refused by the workspace query, on the host."""
+    from helix_online_kv import _build
+    _build.build(verbose=False)
+    lib = _lib.lib()
+    a = _lib.Cdc03Args()
+    a.batch, a.kv_heads, a.q_per_kv, a.head_dim = 1, 1, 4, 64
+    a.n_subspaces, a.sub_dim, a.code_bytes, a.cb_slots = 8, 8, 8, 256
+    a.top_k, a.sink_tokens, a.hot_window, a.scale, a.lut_order = 128, 4, 256, 0.125, _lib.DOT_GEMV
+    dummy = 1 << 20   # never dereferenced: the query only validates
+    a.q = a.out = a.k = a.v = a.codes = a.codebook = a.cb_k = a.seq_len = dummy
+    a.q_dtype = a.out_dtype = a.kv_dtype = _lib.F16
+    a.kv_stride_b = a.kv_stride_h = 0
+    a.code_stride_b = a.code_stride_h = 0
+    need = ctypes.c_size_t(0)
+    a.capacity = 248 * 2048 + 256
+    assert lib.hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need)) == 0 and need.value > 0
+    a.capacity = 248 * 2048 + 256 + 16
+    st = lib.hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need))
+    assert st != 0 and b"chunks" in lib.hokv_last_error()

@@ -267,6 +267,25 @@ def test_ties_and_candidate_overflow():
     _check_store(st, q, [S, S], 0.125, 128, 4, 256, "ties")
 
 
+def test_one_bin_holding_more_than_65535_tokens():
+    """80K identical keys: every score falls in one histogram bin, whose count
+    over the whole cluster passes the 16-bit counters.  The pooled count
+    saturates (the threshold can only drop), every chunk's list overflows and
+    is rescanned exactly, and the selection is the lowest token indices."""
+    from helix_online_kv.cdc03 import CDC03Store
+    B, H, S, D, M = 1, 1, 80000, 64, 8
+    st = CDC03Store(B, 1, H, D, S, n_subspaces=M, dtype=torch.float16)
+    rng = np.random.default_rng(17)
+    row = rng.standard_normal(D).astype(np.float32)
+    st.k[0, 0, 0, :S] = torch.from_numpy(np.tile(row, (S, 1))).half().cuda()
+    st.v[0, 0, 0, :S] = torch.from_numpy(rng.standard_normal((S, D)).astype(np.float32)).half().cuda()
+    st.seq_len.fill_(S)
+    st.calibrate(0, 128)
+    st.assign(0, 0, S)
+    q = torch.from_numpy(rng.standard_normal((B, 2 * H, D)).astype(np.float32)).half().cuda()
+    assert _check_store(st, q, [S], 0.125, 128, 4, 256, "one bin") == 0
+
+
 def test_hot_window_zero_equals_hybrid(golden):
     """hot_window = 0 on the batched store is the reference hybrid_pq_attention."""
     K, V = O.gen_kv(0, 1, 4, 1024, 64)
