@@ -232,6 +232,9 @@ typedef struct hokv_cdc03_args {
   void* workspace; size_t workspace_bytes;
 } hokv_cdc03_args;
 
+/* Scratch bytes the stages below need for `a`.  HOKV_ERR_UNSUPPORTED when
+ * capacity - hot_window exceeds 248 chunks of 2048 tokens (507,904), where the
+ * candidate stage's 16-bit histogram counters could overflow. */
 int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes);
 /* Both stages below, in order, on `stream`. */
 int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream);
