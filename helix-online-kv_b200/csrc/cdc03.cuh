@@ -924,31 +924,44 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     explicit_sel = true;
     const int M = p.M;
     const int64_t cbase_idx = (int64_t)u * p.n_chunks * p.GT;
-    // common case in one memory round trip: at most NW chunks, none with more
-    // than K7_FAST_SLOTS candidates; warp c loads chunk c's count together with
-    // its first K7_FAST_SLOTS list slots and keeps the slots below the count
-    bool fast = p.n_chunks <= NW;
-    int my_cnt = 0;
+    // common case in one memory round trip, the counts read together with the
+    // first list slots (the slots below the count are kept): up to NW chunks,
+    // warp c reads chunk c and its first 64 slots; up to 2 NW chunks, chunks c
+    // and c + NW, 32 slots each
+    const bool two = p.n_chunks > NW;
+    const int slots = two ? K7_FAST_SLOTS / 2 : K7_FAST_SLOTS;
+    bool fast = p.n_chunks <= 2 * NW;
+    int cnt0 = 0, cnt1 = 0;
     uint64_t k0 = 0ull, k1 = 0ull;
-    if (fast && warp < p.n_chunks) {
-      const int64_t li = cbase_idx + (int64_t)warp * p.GT + g;
-      my_cnt = __ldcg(p.cand_cnt + li);
+    const int c0 = warp, c1 = warp + NW;
+    if (fast && c0 < p.n_chunks) {
+      const int64_t li = cbase_idx + (int64_t)c0 * p.GT + g;
+      cnt0 = __ldcg(p.cand_cnt + li);
       k0 = __ldcg(p.cand_key + li * CAND_MAX + lane);
-      k1 = __ldcg(p.cand_key + li * CAND_MAX + lane + 32);
-      if (lane == 0) s_cnt[warp] = my_cnt;
+      if (!two) k1 = __ldcg(p.cand_key + li * CAND_MAX + lane + 32);
+      if (lane == 0) s_cnt[c0] = cnt0;
     }
-    fast = !__syncthreads_or(!fast || (warp < p.n_chunks && (my_cnt < 0 || my_cnt > K7_FAST_SLOTS)));
+    if (fast && two && c1 < p.n_chunks) {
+      const int64_t li = cbase_idx + (int64_t)c1 * p.GT + g;
+      cnt1 = __ldcg(p.cand_cnt + li);
+      k1 = __ldcg(p.cand_key + li * CAND_MAX + lane);
+      if (lane == 0) s_cnt[c1] = cnt1;
+    }
+    fast = !__syncthreads_or(!fast || (c0 < p.n_chunks && (cnt0 < 0 || cnt0 > slots)) ||
+                             (two && c1 < p.n_chunks && (cnt1 < 0 || cnt1 > slots)));
     if (fast) {
-      int off = 0, n_all = 0;
+      int off0 = 0, off1 = 0, n_all = 0;
       for (int c = 0; c < p.n_chunks; ++c) {
         const int x = s_cnt[c];
-        off += c < warp ? x : 0;
+        off0 += c < c0 ? x : 0;
+        off1 += c < c1 ? x : 0;
         n_all += x;
       }
-      if (warp < p.n_chunks) {
-        if (lane < my_cnt) keys[off + lane] = k0;
-        if (lane + 32 < my_cnt) keys[off + lane + 32] = k1;
+      if (c0 < p.n_chunks) {
+        if (lane < cnt0) keys[off0 + lane] = k0;
+        if (!two && lane + 32 < cnt0) keys[off0 + lane + 32] = k1;
       }
+      if (two && c1 < p.n_chunks && lane < cnt1) keys[off1 + lane] = k1;
       for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
       if (tid < 4) keys[n_all + tid] = 0ull;   // padding to a multiple of 4: a zero key beats none
       if (tid == 0) s_n = min(n_all, cr.kp);

@@ -204,6 +204,15 @@ def test_store_16k_list_sizes(top_k):
     assert _check_store(st, q, lens, 0.125, top_k, 4, 256, f"16k top{top_k}") <= 4
 
 
+@pytest.mark.parametrize("top_k", [128, 500])
+def test_store_30k_two_chunks_per_warp(top_k):
+    """30K tokens, 15 chunks: the attention stage reads two chunks per warp
+    with 32 list slots each; top-500 leaves more than 32 candidates in some
+    chunks, which then take the counts-first path."""
+    st, q, lens = _store(1, 1, 2, 64, 30000, 8, torch.float16, seed=37)
+    assert _check_store(st, q, lens, 0.125, top_k, 4, 256, f"30k top{top_k}") <= 4
+
+
 def test_store_more_than_128_live_centroids():
     """Codebooks calibrated on 300 tokens keep up to 256 live centroids per
     subspace: the candidate stage reads the rows past the first 128 in a
