@@ -67,6 +67,13 @@ def _traffic_from_profiles(kernel: str):
 
 
 # ----------------------------------------------------------------------------- reference arm (CPU)
+def config_for(w: dict, world: int) -> dict:
+    """The workload's `config` object, identical in both arms."""
+    step_bytes_note = "inputs larger than L2 (16.6 GB of K/V per GPU, 126 MB L2); no flush needed"
+    return dict(w, global_batch=w["batch_per_gpu"] * world, parallelism=f"sequence-sharded x{world}",
+                l2=step_bytes_note)
+
+
 def _ref_unit(seed: int, S: int, D: int, M: int, G: int):
     from oracle import hokv_oracle as O
     K, V = O.gen_kv(seed, 1, 1, S, D)
@@ -78,63 +85,93 @@ def _ref_unit(seed: int, S: int, D: int, M: int, G: int):
     return K, V, codes, cents, Q
 
 
-def _ref_worker(args):
-    seed, n_queries, S, D, M, G, top_k, sink, hot = args
+def _ref_worker(seed, shape, per_step, n_steps, barrier, results):
+    """One host core: builds its own (sequence, KV head) unit once, then at every
+    step, between two barriers, runs `per_step` CDC-03 head-queries on it."""
+    S, D, M, G, top_k, sink, hot = shape
     from oracle import hokv_oracle as O
-    global _REF_CACHE
-    try:
-        _REF_CACHE
-    except NameError:
-        _REF_CACHE = {}
-    if seed not in _REF_CACHE:
-        _REF_CACHE[seed] = _ref_unit(seed, S, D, M, G)
-    K, V, codes, cents, Q = _REF_CACHE[seed]
+    K, V, codes, cents, Q = _ref_unit(seed, S, D, M, G)
     scale = 1.0 / np.sqrt(D)
-    t0 = time.perf_counter()
-    for i in range(n_queries):
-        O.cdc03_hot_attention(Q[i % G], K, V, codes, cents, scale, top_k, sink, hot)
-    return n_queries, time.perf_counter() - t0
+    times = []
+    for _ in range(n_steps):
+        barrier.wait(timeout=600)
+        t0 = time.perf_counter()
+        for i in range(per_step):
+            O.cdc03_hot_attention(Q[i % G], K, V, codes, cents, scale, top_k, sink, hot)
+        times.append(time.perf_counter() - t0)
+        barrier.wait(timeout=600)
+    results.put(times)
 
 
-def cpu_rate(n_workers: int, per_worker: int, reps: int, S: int, D: int, M: int, G: int, w):
-    """Head-queries/s of the oracle's CDC-03 (numpy) on n_workers processes."""
+def cpu_rate(n_workers: int, per_step: int, n_steps: int, shape):
+    """Wall-clock seconds of each step of `n_workers` processes (one BLAS thread
+    each) running `per_step` head-queries apiece of the oracle's CDC-03; a step
+    runs from the barrier that releases every worker to the barrier that the
+    last of them reaches.  shape = (S, D, M, G, top_k, sink, hot)."""
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
-    # one BLAS thread per worker process (the workers read these when they import numpy)
     for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
-        os.environ[var] = "1"
-    jobs = [(1000 + i, per_worker, S, D, M, G, w["top_k"], w["sink_tokens"], w["hot_window"])
-            for i in range(n_workers)]
-    with ctx.Pool(n_workers) as pool:
-        pool.map(_ref_worker, [(j[0], 1) + j[2:] for j in jobs])  # build per-worker data, warm
-        rates = []
-        for _ in range(reps):
+        os.environ[var] = "1"   # read by each worker's numpy at import
+    barrier = ctx.Barrier(n_workers + 1)
+    results = ctx.Queue()
+    procs = [ctx.Process(target=_ref_worker, args=(1000 + i, shape, per_step, n_steps, barrier, results), daemon=True)
+             for i in range(n_workers)]
+    for pr in procs:
+        pr.start()
+    steps = []
+    try:
+        for _ in range(n_steps):
+            barrier.wait(timeout=900)   # the first pass waits for every worker's unit
             t0 = time.perf_counter()
-            res = pool.map(_ref_worker, jobs)
-            dt = time.perf_counter() - t0
-            rates.append(sum(r[0] for r in res) / dt)
-    return rates
+            barrier.wait(timeout=900)
+            steps.append(time.perf_counter() - t0)
+        worker_times = [results.get(timeout=120) for _ in procs]
+    finally:
+        for pr in procs:
+            pr.join(timeout=30)
+            if pr.is_alive():
+                pr.terminate()
+    return steps, worker_times
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
-    w = WORKLOAD
-    cores = os.cpu_count() or 1
-    per_step = 16
-    rates = cpu_rate(cores, per_step, args.warmup + args.steps, w["context"], w["head_dim"], w["pq_subspaces"],
-                     w["q_heads"] // w["kv_heads"], w)
-    timed = rates[args.warmup:]
+    w = dict(WORKLOAD)
+    if args.layers:
+        w["layers"] = args.layers
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    G = w["q_heads"] // w["kv_heads"]
+    shape = (w["context"], w["head_dim"], w["pq_subspaces"], G, w["top_k"], w["sink_tokens"], w["hot_window"])
     hq_per_token = w["layers"] * w["q_heads"]
-    tok_s = statistics.median(timed) / hq_per_token
+    step_hq = w["batch_per_gpu"] * world * hq_per_token          # head-queries of one decode step
+    per_worker = min(-(-step_hq // cores), args.ref_cap)
+    # one core alone first (same per-worker sample), then every core
+    one_steps, _ = cpu_rate(1, per_worker, 2, shape)
+    one_rate = per_worker / min(one_steps)
+    steps, _ = cpu_rate(cores, per_worker, args.warmup + args.steps, shape)
+    timed = steps[args.warmup:]
+    step_s = statistics.median(timed)
+    rate = cores * per_worker / step_s                            # head-queries/s, all cores
+    tok_s = rate / hq_per_token
+    sample = (f"{cores} processes (one per host core, one BLAS thread each) x {per_worker} head-queries per step "
+              f"at S={w['context']}, D={w['head_dim']}, M={w['pq_subspaces']}: "
+              + ("the whole decode step" if per_worker * cores >= step_hq else
+                 f"a sample of {per_worker * cores} of the step's {step_hq} head-queries")
+              + f"; one core alone: {one_rate:.1f} head-queries/s")
     line = {
-        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / tok_s, "higher_is_better": True,
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32 (numpy)", "data": "synthetic",
-        "config": dict(w, note="CPU oracle restatement of the reference's numpy hybrid_pq_attention with a hot window"),
-        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{cores} processes x {per_step} head-queries per step at S=16384"},
+        "config": config_for(w, world),
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample,
+                         "single_core_value": one_rate / hq_per_token,
+                         "parallel_efficiency": rate / (cores * one_rate),
+                         "impl_note": "the oracle's restatement of the reference's numpy hybrid_pq_attention "
+                                      "(compressed_attention.py:315-412) with the hot window"},
+        "ms_per_step_min": min(timed) * 1e3, "ms_per_step_max": max(timed) * 1e3,
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -212,13 +249,74 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _time_graph(graph, n, barrier):
+    """Device milliseconds of `n` replays of `graph`, between barriers."""
+    import torch
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def _check_against_oracle(store, q, out, layers, units, scale, top_k, sink, hot):
+    """The decode outputs of `units` (b, h) of `layers` against the oracle: PQ
+    codes bit-exact, selected sets exact up to documented near-ties, outputs
+    within max-abs 1e-2 and cosine 0.9999.  Raises RuntimeError on a mismatch."""
+    import torch
+    from oracle import hokv_oracle as O
+    S, M, G = int(store.seq_len[0].item()), store.M, q.shape[2] // store.H
+    worst, ties = 0.0, 0
+    for l in layers:
+        o_dev, (sel, _, cnt) = store.decode(l, q[l], scale, top_k, sink, hot, out_dtype=torch.float32,
+                                            return_selection=True)
+        for b, h in units:
+            Kh = store.k[l, b, h, :S].float().cpu().numpy()
+            Vh = store.v[l, b, h, :S].float().cpu().numpy()
+            kk = store.cb_k[l, b, h].cpu().numpy()
+            cb = store.codebook[l, b, h].cpu().numpy()
+            cents = [cb[s_, :kk[s_]] for s_ in range(M)]
+            codes = store.codes[l, b, h, :S, :M].cpu().numpy()
+            if not np.array_equal(codes[:S - hot], O.pq_assign(Kh[:S - hot], cents)):
+                raise RuntimeError(f"check failed: layer {l} unit {(b, h)}: PQ codes differ from the oracle")
+            for g in range(G):
+                hq = h * G + g
+                qv = q[l, b, hq].float().cpu().numpy()
+                rsel, _, rout = O.cdc03_hot_attention(qv, Kh, Vh, codes, cents, scale, top_k, sink, hot)
+                got = np.sort(sel[b, hq, :int(cnt[b, hq])].cpu().numpy())
+                if not np.array_equal(got, rsel):
+                    approx = O.pq_gather(O.pq_tables(qv, cents), codes[:S - hot]) * np.float32(scale)
+                    diff = np.setxor1d(got, rsel)
+                    masked = approx.astype(np.float64)
+                    masked[:sink] = -np.inf
+                    bound = np.sort(masked)[-(top_k - sink)]
+                    tol = 8 * np.spacing(np.float32(abs(bound)))
+                    if len(diff) > 4 or any(abs(float(approx[t]) - bound) > tol for t in diff):
+                        raise RuntimeError(f"check failed: layer {l} head {(b, hq)}: selection differs {diff}")
+                    ties += len(diff)
+                o = o_dev[b, hq].cpu().numpy()
+                err = float(np.max(np.abs(o - rout)))
+                worst = max(worst, err)
+                if err > 1e-2 or O.cosine(o, rout) < 0.9999:
+                    raise RuntimeError(f"check failed: layer {l} head {(b, hq)}: max-abs {err}")
+                # the timed step's own output for this head (stored bf16: 2^-8 relative
+                # rounding) agrees with the fp32 re-run
+                if not torch.allclose(out[l, b, hq].float().cpu(), o_dev[b, hq].cpu(), atol=1e-2, rtol=2.0 ** -8):
+                    raise RuntimeError(f"check failed: layer {l} head {(b, hq)}: timed output differs")
+    return {"layers": list(layers), "units": [list(u) for u in units], "head_queries": len(layers) * len(units) * G,
+            "max_abs": worst, "near_tie_tokens": ties, "passed": True}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     from helix_online_kv import _lib as L
     from helix_online_kv.cdc03 import CDC03Store
-    from helix_online_kv.sharding import max_over_ranks
+    from helix_online_kv.sharding import gather_outputs, max_over_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -259,25 +357,37 @@ def run_ours(args):
             if st:
                 L.check(st, "cdc03_decode")
 
-    # eager warm-up (sets kernel attributes), then capture one step in a graph
+    def api_step():
+        # the public Python API a model calls, one layer after another
+        for l in range(Ls):
+            store.decode(l, q[l], scale, top_k, sink, hot, out=out[l])
+
+    # eager warm-up (sets kernel attributes, sizes the workspace), then one step in a graph
     step(L.stream())
+    api_step()
     torch.cuda.synchronize()
     L.device_status()
-    graph = torch.cuda.CUDAGraph()
     cap_stream = torch.cuda.Stream()
-    cap_stream.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(cap_stream):
-        with torch.cuda.graph(graph, stream=cap_stream):
-            step(L.stream())
-    torch.cuda.current_stream().wait_stream(cap_stream)
-    torch.cuda.synchronize()
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        cap_stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap_stream):
+            with torch.cuda.graph(g, stream=cap_stream):
+                fn()
+        torch.cuda.current_stream().wait_stream(cap_stream)
+        torch.cuda.synchronize()
+        return g
+
+    graph = capture(lambda: step(L.stream()))
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(max(args.warmup, 3)):
+    warm = max(args.warmup, 3)
+    for _ in range(warm):
         graph.replay()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -287,7 +397,10 @@ def run_ours(args):
             graph.replay()
         ev1.record()
         torch.cuda.synchronize()
+        # the same K-step region again, for the spread of the measurement
+        repeats = [_time_graph(graph, args.steps, barrier) for _ in range(args.repeats)]
     ms = max_over_ranks(ev0.elapsed_time(ev1), device="cuda")
+    repeats = [max_over_ranks(r, device="cuda") / args.steps for r in repeats]
     barrier()
     ms_step = ms / args.steps
     tokens = B * world * args.steps
@@ -299,22 +412,12 @@ def run_ours(args):
     n_att = max(3, min(args.steps, 10))
 
     def stage_ms(fn, name):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(cap_stream):
-            with torch.cuda.graph(g, stream=cap_stream):
-                for r in refs:
-                    L.check(fn(r, L.stream()), name)
-        torch.cuda.synchronize()
+        g = capture(lambda: [L.check(fn(r, L.stream()), name) for r in refs])
         g.replay()
         torch.cuda.synchronize()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(n_att):
-            g.replay()
-        t1.record()
-        torch.cuda.synchronize()
+        t = _time_graph(g, n_att, torch.cuda.synchronize)
         del g
-        return t0.elapsed_time(t1) / (n_att * Ls)
+        return t / (n_att * Ls)
 
     k6_ms = stage_ms(lib.hokv_cdc03_candidates, "candidates")
     k7_ms = stage_ms(lib.hokv_cdc03_attend, "attend")
@@ -343,26 +446,42 @@ def run_ours(args):
 
     step_bytes = (k6_bytes + k7_bytes) * Ls
 
-    # end-to-end through the public API: host (pinned) queries in, host outputs out
+    # end to end through the public API (CDC03Store.decode per layer): pinned host
+    # queries in, host outputs out, every step; captured in a graph (as a serving
+    # loop would), and eager; at N > 1 every step also all-gathers the last
+    # layer's outputs of every rank over NCCL
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    for _ in range(2):
-        q.copy_(q_host, non_blocking=True)
-        graph.replay()
-        out_host.copy_(out, non_blocking=True)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        q.copy_(q_host, non_blocking=True)
-        graph.replay()
-        out_host.copy_(out, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), device="cuda")
-    e2e_value = tokens / (e2e_ms / 1e3)
+    api_graph = capture(api_step)
+    gathered_host = None
+    if world > 1:
+        gathered_host = torch.empty((B * world, Hq, D), dtype=out.dtype).pin_memory()
 
-    # VQ-assign throughput: PQ codes for a fresh 32768-token block of every (b, h) of one layer
+    def e2e_loop(n, use_graph):
+        for _ in range(n):
+            q.copy_(q_host, non_blocking=True)
+            if use_graph:
+                api_graph.replay()
+            else:
+                api_step()
+            out_host.copy_(out, non_blocking=True)
+            if world > 1:
+                gathered_host.copy_(gather_outputs(out[Ls - 1]), non_blocking=True)
+
+    e2e = {}
+    for name, use_graph in (("graph", True), ("eager", False)):
+        e2e_loop(2, use_graph)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        e2e_loop(args.steps, use_graph)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e[name] = max_over_ranks(e0.elapsed_time(e1), device="cuda")
+    h2d = q.numel() * q.element_size()
+    d2h = out.numel() * out.element_size() + (gathered_host.numel() * gathered_host.element_size() if world > 1 else 0)
+
+    # VQ-assign throughput: PQ codes for a fresh 8192-token block of every (b, h) of one layer
     n_new = 8192
     torch.cuda.synchronize()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -375,12 +494,17 @@ def run_ours(args):
     as_ms = a0.elapsed_time(a1) / 3
     as_bytes = units * n_new * (D * 2 + M)
     as_gbs = as_bytes / (as_ms * 1e-3) / 1e9
+    graph.replay()
+    torch.cuda.synchronize()
 
-    # CPU baseline: the oracle on one host core, bounded sample (rank 0, N=1)
-    cpu = None
+    # CPU baseline (rank 0, N=1): the oracle on one host core, bounded sample;
+    # the same leg checks the timed step's outputs of a few units against it
+    cpu, check = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import hokv_oracle as O
-        reps, n_q, t_cpu = 0, 0, 0.0
+        check = _check_against_oracle(store, q, out, sorted({0, Ls - 1}), [(0, 0), (B - 1, H - 1)], scale, top_k,
+                                      sink, hot)
+        reps, t_cpu = 0, 0.0
         Kh = store.k[0, 0, 0, :S].float().cpu().numpy()
         Vh = store.v[0, 0, 0, :S].float().cpu().numpy()
         kk = store.cb_k[0, 0, 0].cpu().numpy()
@@ -402,24 +526,36 @@ def run_ours(args):
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": warm, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8 codes + fp32 exact scoring (bf16 K/V)", "data": "synthetic",
-        "config": dict(w, global_batch=B * world, parallelism=f"sequence-sharded x{world}",
-                       l2="inputs larger than L2 (%.2f GB algorithmic per step)" % (step_bytes / 1e9)),
+        "config": config_for(w, world),
+        "value_per_gpu": value / world,
+        "spread": {"repeats": args.repeats, "steps_each": args.steps,
+                   "ms_per_step_median": statistics.median(repeats) if repeats else None,
+                   "ms_per_step_min": min(repeats) if repeats else None,
+                   "ms_per_step_max": max(repeats) if repeats else None},
         "roofline": roof(dom), "roofline_other": roof(other),
         "step_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9, "step_frac": step_bytes / (ms_step * 1e-3) / 1e9 / peak,
+        "step_algorithmic_bytes": step_bytes,
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": q.numel() * q.element_size(),
-                "d2h_bytes_per_step": out.numel() * out.element_size()},
+        "e2e": {"value": tokens / (e2e["graph"] / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "CDC03Store.decode for every layer (captured in a CUDA graph), pinned H2D of the queries "
+                        "and D2H of the outputs every step"
+                        + ("; NCCL all-gather of the last layer's outputs of every rank every step" if world > 1
+                           else "")},
+        "e2e_eager": {"value": tokens / (e2e["eager"] / 1e3), "unit": "tokens/s",
+                      "path": "the same calls without a graph (host launch cost included)"},
         "vq_assign": {"value": as_gbs, "unit": "GB/s", "frac": as_gbs / peak, "vectors": units * n_new,
                       "ms": as_ms, "kernel": "k_pq_assign_seq (fp32 CUDA cores, 4 vectors per thread in registers)"},
         "gpu_launches": args.steps * Ls * 2,   # k6_candidates + k7_select_attend per layer
+        "check": check,
         "clocks": clk.summary(),
         "setup_s": t_setup,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, api_graph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -433,7 +569,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-cap", type=int, default=512,
+                    help="reference arm: most head-queries per host core in one step (bounds a step's time)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--repeats", type=int, default=10,
+                    help="after the timed region, time the same K steps this many more times (spread)")
     ap.add_argument("--layers", type=int, default=0,
                     help="layers to run (default: the workload's 31); fewer only for profiler captures, "
                          "whose JSON line is then not the workload's")

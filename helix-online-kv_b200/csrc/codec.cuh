@@ -1,7 +1,7 @@
 // codec.cuh -- codebook calibration and nearest-centroid assignment.
 //
 // Reference semantics (helix_online_kv):
-//  * OnlineCodebook (codebook.py:97-261): k = min(n_clusters, #unique values),
+//  * OnlineCodebook (codebook.py:57-221): k = min(n_clusters, #unique values),
 //    np.percentile init, Lloyd with argmin |x - c| (first minimum) and
 //    per-cluster np.mean, stop when max |shift| < rtol * (c[-1] - c[0]).
 //  * VectorCodebook (vector_codebook.py:95-242): k = min(n_clusters, #unique
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(1024) k_scalar_kmeans(const float* __restrict_
   }
 }
 
-// EMA drift step for one codebook (codebook.py:204-216): one CTA.
+// EMA drift step for one codebook (codebook.py:146-176): one CTA.
 __global__ void __launch_bounds__(1024) k_scalar_ema(const float* __restrict__ vals, int64_t n,
                                                      float* __restrict__ cents, int k, float alpha,
                                                      uint8_t* __restrict__ asg, float* __restrict__ mem) {

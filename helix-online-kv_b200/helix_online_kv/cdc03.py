@@ -56,6 +56,8 @@ class CDC03Store:
         self.cb_k = torch.zeros((n_layers, batch, kv_heads, n_subspaces), dtype=torch.int32, device=dev)
         self.seq_len = torch.zeros(batch, dtype=torch.int32, device=dev)
         self._ws = None
+        self._args_cache = {}   # decode arguments by (layer, tensors, budgets): no per-call rebuild
+        self._ws_need = {}      # workspace bytes by (group, budgets)
 
     # ---- calibration and assignment -----------------------------------------
     def calibrate(self, layer: int, n_tokens: int = 128, sub_clusters: int = 256, max_iters: int = 30,
@@ -164,9 +166,30 @@ class CDC03Store:
     # ---- decode ---------------------------------------------------------------
     def args(self, layer: int, q, out, scale: float, top_k: int = 128, sink_tokens: int = 4,
              hot_window: int = 256, sel_idx=None, sel_score=None, sel_count=None) -> L.Cdc03Args:
+        """The C-ABI arguments of one layer's decode.  Built once per (layer,
+        tensors, budgets) and kept: a decode step repeats the same calls, and the
+        structure holds only device addresses and sizes."""
+        ptr = lambda t: None if t is None else t.data_ptr()   # noqa: E731
+        key = (layer, q.data_ptr(), q.dtype, tuple(q.shape), tuple(q.stride()), out.data_ptr(), out.dtype,
+               tuple(out.stride()), float(scale), int(top_k), int(sink_tokens), int(hot_window), ptr(sel_idx),
+               ptr(sel_score), ptr(sel_count))
+        a = self._args_cache.get(key)
+        if a is not None and self._ws is not None and a.workspace == self._ws.data_ptr():
+            return a
+        if len(self._args_cache) > 1024:
+            self._args_cache.clear()
+        a = self._build_args(layer, q, out, scale, top_k, sink_tokens, hot_window, sel_idx, sel_score, sel_count)
+        self._args_cache[key] = a
+        return a
+
+    def _build_args(self, layer, q, out, scale, top_k, sink_tokens, hot_window, sel_idx, sel_score, sel_count):
         B, Hq, D = q.shape
         if B != self.B or D != self.D or Hq % self.H:
             raise ValueError(f"queries {tuple(q.shape)} do not match the store (B={self.B}, H_kv={self.H}, D={self.D})")
+        if q.stride(2) != 1 or q.stride(1) != D or out.shape != q.shape or out.stride(2) != 1 or out.stride(1) != D:
+            raise ValueError("queries and outputs must be [B, H_q, D] with contiguous heads")
+        if not 0 <= layer < self.L:
+            raise ValueError(f"layer {layer} outside 0..{self.L - 1}")
         a = L.Cdc03Args()
         a.batch, a.kv_heads, a.q_per_kv, a.head_dim = self.B, self.H, Hq // self.H, self.D
         a.n_subspaces, a.sub_dim, a.code_bytes, a.cb_slots = self.M, self.sd, self.CS, SLOTS
@@ -188,10 +211,15 @@ class CDC03Store:
         a.sel_idx = sel_idx.data_ptr() if sel_idx is not None else None
         a.sel_score = sel_score.data_ptr() if sel_score is not None else None
         a.sel_count = sel_count.data_ptr() if sel_count is not None else None
-        need = ctypes.c_size_t(0)
-        L.check(L.lib().hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need)), "cdc03_workspace_size")
-        if self._ws is None or self._ws.numel() < need.value:
-            self._ws = L.workspace(need.value)
+        wkey = (a.q_per_kv, a.top_k, a.sink_tokens, a.hot_window)
+        need = self._ws_need.get(wkey)
+        if need is None:
+            n = ctypes.c_size_t(0)
+            L.check(L.lib().hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(n)), "cdc03_workspace_size")
+            need = self._ws_need[wkey] = n.value
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = L.workspace(need)
+            self._args_cache.clear()   # earlier arguments point at the old workspace
         a.workspace, a.workspace_bytes = self._ws.data_ptr(), self._ws.numel()
         return a
 

@@ -35,7 +35,7 @@ def _flat_dev(values):
 class OnlineCodebook:
     """Scalar codebook: ``feed_calibration`` -> ``finalize_calibration`` -> ``assign``.
 
-    Lifecycle and errors as in codebook.py:48-216.
+    Lifecycle and errors as in codebook.py:47-176.
     """
 
     def __init__(self, n_clusters: int = 256, max_iters: int = 10, rtol: float = 0.001,
@@ -68,7 +68,7 @@ class OnlineCodebook:
         self._centroids = dev.cpu().numpy()
 
     def feed_calibration(self, values) -> None:
-        """Accumulate calibration values (codebook.py:87-95)."""
+        """Accumulate calibration values (codebook.py:47-55)."""
         if self._finalized:
             raise RuntimeError("Codebook already finalized")
         if _is_tensor(values):
@@ -77,7 +77,7 @@ class OnlineCodebook:
             self._calibration_buffer.append(np.asarray(values).ravel().astype(np.float32))
 
     def finalize_calibration(self) -> dict:
-        """Fit the codebook on the device (codebook.py:97-124, 218-261)."""
+        """Fit the codebook on the device (codebook.py:57-84, 178-221)."""
         if self._finalized:
             raise RuntimeError("Codebook already finalized")
         if not self._calibration_buffer:
@@ -93,7 +93,7 @@ class OnlineCodebook:
                 "n_iters": int(stats["iters"][0]), "calibration_mse": float(stats["mse"][0])}
 
     def assign(self, values):
-        """Nearest centroid (first minimum) as uint8 (codebook.py:126-139)."""
+        """Nearest centroid (first minimum) as uint8 (codebook.py:86-99)."""
         if not self._finalized:
             raise RuntimeError("Codebook not finalized — call finalize_calibration() first")
         x = _flat_dev(values)
@@ -105,7 +105,7 @@ class OnlineCodebook:
         return out if _is_tensor(values) else out.cpu().numpy()
 
     def decode(self, indices):
-        """centroids[indices] (codebook.py:141-152)."""
+        """centroids[indices] (codebook.py:101-112)."""
         if not self._finalized:
             raise RuntimeError("Codebook not finalized")
         idx = indices if _is_tensor(indices) else L.to_dev(np.asarray(indices), torch.uint8)
@@ -123,12 +123,12 @@ class OnlineCodebook:
         return recon_stats(x, r.reshape(-1).contiguous())
 
     def quantization_error(self, values, indices) -> float:
-        """MSE of the reconstruction in NumPy's float32 order (codebook.py:154-165)."""
+        """MSE of the reconstruction in NumPy's float32 order (codebook.py:114-125)."""
         s = self._stats(values, indices)
         return float(np.float32(s["sse"] / s["n"]))
 
     def cosine_similarity(self, values, indices) -> float:
-        """Cosine between values and reconstruction (codebook.py:167-184)."""
+        """Cosine between values and reconstruction (codebook.py:127-144)."""
         s = self._stats(values, indices)
         na, nb = np.sqrt(s["xx"]), np.sqrt(s["rr"])
         if na < 1e-30 or nb < 1e-30:
@@ -136,7 +136,7 @@ class OnlineCodebook:
         return float(s["xr"] / (na * nb))
 
     def maybe_update_centroids(self, values, error: float) -> bool:
-        """EMA drift correction when error exceeds the threshold (codebook.py:186-216)."""
+        """EMA drift correction when error exceeds the threshold (codebook.py:146-176)."""
         if not self._finalized:
             return False
         if error <= self.drift_threshold:

@@ -57,7 +57,7 @@ int hokv_device_status(void* stream);
  * Scalar codebook (Path A / layer state)
  * ---------------------------------------------------------------------- */
 
-/* OnlineCodebook.assign -- codebook.py:126-139.  argmin_j |x - c_j| with the
+/* OnlineCodebook.assign -- codebook.py:86-99.  argmin_j |x - c_j| with the
  * first minimum, x given as f32/f16/bf16 (`dtype`).  n_sets independent
  * problems: values[set*values_stride + i], centroids[set*cent_stride + j],
  * out[set*out_stride + i]. */
@@ -65,11 +65,11 @@ int hokv_scalar_assign(const void* values, int dtype, int64_t n, int64_t values_
                        const float* centroids, int k, int64_t cent_stride,
                        uint8_t* out, int64_t out_stride, int n_sets, void* stream);
 
-/* OnlineCodebook.decode -- codebook.py:141-152 (out = centroids[idx]). */
+/* OnlineCodebook.decode -- codebook.py:101-112 (out = centroids[idx]). */
 int hokv_scalar_decode(const uint8_t* idx, int64_t n, const float* centroids, int k,
                        float* out, void* stream);
 
-/* OnlineCodebook.finalize_calibration + _fit_kmeans -- codebook.py:97-124,218-261.
+/* OnlineCodebook.finalize_calibration + _fit_kmeans -- codebook.py:57-84,178-221.
  * n_sets independent 1-D k-means fits over data[set*data_stride + i], i < n.
  * Per set writes centroids[set*n_clusters + j] (j < k), k_out[set],
  * iters_out[set], mse_out[set] (f64) and, if non-NULL, the last assignment
@@ -81,14 +81,14 @@ int hokv_scalar_kmeans(const float* data, int64_t n, int64_t data_stride, int n_
                        uint8_t* assign_out, void* workspace, size_t workspace_bytes,
                        void* stream);
 
-/* OnlineCodebook.maybe_update_centroids EMA step -- codebook.py:186-216 (the
+/* OnlineCodebook.maybe_update_centroids EMA step -- codebook.py:146-176 (the
  * caller applies the drift threshold).  centroids updated in place. */
 int hokv_scalar_ema(const float* values, int64_t n, float* centroids, int k, float alpha,
                     void* workspace, size_t workspace_bytes, void* stream);
 size_t hokv_scalar_ema_workspace_size(int64_t n);
 
 /* quantization_error / cosine_similarity of all three codebooks
- * (codebook.py:154-184, vector_codebook.py:166-181, product_codebook.py:229-250):
+ * (codebook.py:114-144, vector_codebook.py:166-183, product_codebook.py:231-250):
  * out4[0] = sum((x - r)^2) in numpy's float32 pairwise order, out4[1] = x.r,
  * out4[2] = |x|^2, out4[3] = |r|^2 (f64).  r is given densely; the workspace
  * holds n floats. */

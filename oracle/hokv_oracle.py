@@ -70,13 +70,13 @@ def to_fp16_values(x):
 
 
 def scalar_assign(values, centroids):
-    """argmin_j |x - c_j| (first minimum) as uint8.  codebook.py:126-139."""
+    """argmin_j |x - c_j| (first minimum) as uint8.  codebook.py:86-99."""
     flat = np.asarray(values).ravel().astype(F32)
     return np.argmin(np.abs(flat[:, None] - centroids), axis=1).astype(np.uint8)
 
 
 def scalar_fit(data, n_clusters: int = 256, max_iters: int = 10, rtol: float = 1e-3):
-    """1-D k-means with percentile init.  codebook.py:218-261.
+    """1-D k-means with percentile init.  codebook.py:178-221.
 
     Returns ``(centroids f32 [k], assignments u8 [N], n_iters)``; the
     assignments are those of the last assignment step, as in the reference.
@@ -102,7 +102,7 @@ def scalar_fit(data, n_clusters: int = 256, max_iters: int = 10, rtol: float = 1
 
 
 def scalar_finalize_stats(data, cents, assign, n_iters):
-    """Stats dict of OnlineCodebook.finalize_calibration (codebook.py:111-124)."""
+    """Stats dict of OnlineCodebook.finalize_calibration (codebook.py:57-84)."""
     data = np.asarray(data, F32).ravel()
     mse = float(np.mean((data - cents[assign]) ** 2))
     return {"n_samples": len(data), "n_clusters": len(cents), "n_iters": n_iters,
@@ -110,7 +110,7 @@ def scalar_finalize_stats(data, cents, assign, n_iters):
 
 
 def scalar_ema_update(values, centroids, alpha: float):
-    """EMA drift correction of codebook.py:204-216 (caller checks the threshold)."""
+    """EMA drift correction of codebook.py:146-176 (caller checks the threshold)."""
     flat = np.asarray(values).ravel().astype(F32)
     idx = scalar_assign(flat, centroids)
     out = centroids.copy()

@@ -1,4 +1,5 @@
-"""bench.py's reference arm on CPU: one JSON line with the contract's keys."""
+"""bench.py's reference arm on CPU: one JSON line with the contract's keys,
+a measured step time, and host cores that really work in parallel."""
 
 import json
 import os
@@ -6,11 +7,13 @@ import subprocess
 import sys
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
 
 
 def test_reference_arm_json_line():
-    r = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
-                        "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=REPO)
+    r = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "2",
+                        "--warmup", "1", "--ref-cap", "64"], capture_output=True, text=True, timeout=900, cwd=REPO)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -19,6 +22,28 @@ def test_reference_arm_json_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["value"] > 0 and d["unit"] == "tokens/s"
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["single_core_value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
     assert d["config"]["workload"] == "cdc03_decode_llama3_8b_kv_16k"
+    # the step time is measured: the rate it implies is the line's value
+    w = d["config"]
+    per_worker = min(-(-w["global_batch"] * w["layers"] * w["q_heads"] // cb["cores"]), 64)
+    implied = cb["cores"] * per_worker / (d["ms_per_step"] / 1e3) / (w["layers"] * w["q_heads"])
+    assert abs(implied / d["value"] - 1) < 1e-6
+    assert d["ms_per_step_min"] <= d["ms_per_step"] <= d["ms_per_step_max"]
+
+
+def test_reference_workers_run_in_parallel():
+    """Two host processes finish a step in about the time one takes: the arm
+    measures parallel work, not data building or dispatch."""
+    import bench
+    if len(os.sched_getaffinity(0)) < 2:
+        import pytest
+        pytest.skip("one host core")
+    shape = (2048, 64, 8, 4, 128, 4, 256)
+    one, _ = bench.cpu_rate(1, 60, 3, shape)
+    two, _ = bench.cpu_rate(2, 60, 3, shape)
+    r1 = 60 / min(one)
+    r2 = 2 * 60 / min(two)
+    assert r2 >= 1.6 * r1, (r1, r2)

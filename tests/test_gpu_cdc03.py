@@ -394,3 +394,11 @@ def test_store_checkpoint_resume(tmp_path):
     assert torch.equal(out1, out2)
     with pytest.raises(ValueError, match="Expected shape"):
         CDC03Store(2, 1, 2, 64, 1024, n_subspaces=8, dtype=torch.float16).load_state_dict(torch.load(path))
+
+
+def test_store_128k_tinyllama_geometry():
+    """128K-token contexts at the TinyLlama KV geometry (G = 8 query heads per
+    KV head, D = 64, M = 8): 63 chunks of 2048 tokens per unit, eight per CTA of
+    the cluster, ragged lengths (131072 and 100000)."""
+    st, q, lens = _store(2, 1, 8, 64, 131072, 8, torch.float16, seed=43, seq_lens=[131072, 100000])
+    assert _check_store(st, q, lens, 0.125, 128, 4, 256, "128k") <= 4
