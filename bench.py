@@ -89,6 +89,9 @@ def _ref_worker(seed, shape, per_step, n_steps, barrier, results):
     """One host core: builds its own (sequence, KV head) unit once, then at every
     step, between two barriers, runs `per_step` CDC-03 head-queries on it."""
     S, D, M, G, top_k, sink, hot = shape
+    cpus = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else []
+    if cpus:   # one worker per host core, kept there
+        os.sched_setaffinity(0, {cpus[(seed - 1000) % len(cpus)]})
     from oracle import hokv_oracle as O
     K, V, codes, cents, Q = _ref_unit(seed, S, D, M, G)
     scale = 1.0 / np.sqrt(D)
@@ -562,6 +565,70 @@ def run_ours(args):
     return 0
 
 
+K6_PHASES = ["rows+queries staged", "dots", "ranges exchanged", "own image entries", "cluster image barrier",
+             "image to smem", "score own chunks", "pool histograms", "threshold", "list+rescore"]
+K7_PHASES = ["hot window", "wait for k6", "selection", "attend selected", "combine+store"]
+
+
+def run_phase_stamps(args):
+    """One decode step of the workload with the profiling build of the library:
+    per-phase durations of the last layer's two kernels from %globaltimer stamps
+    (thread 0 of every CTA), as a JSON line."""
+    import torch
+
+    from helix_online_kv import _lib as L
+    from helix_online_kv.cdc03 import CDC03Store
+    torch.cuda.set_device(0)
+    L.require_device()
+    w = dict(WORKLOAD)
+    if args.layers:
+        w["layers"] = args.layers
+    B, Ls, H, Hq, D, S, M = (w["batch_per_gpu"], w["layers"], w["kv_heads"], w["q_heads"], w["head_dim"],
+                             w["context"], w["pq_subspaces"])
+    top_k, sink, hot = w["top_k"], w["sink_tokens"], w["hot_window"]
+    scale = 1.0 / np.sqrt(D)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234)
+    store = CDC03Store(B, Ls, H, D, S, n_subspaces=M, dtype=torch.bfloat16)
+    for layer in range(Ls):
+        _fill_layer(store, layer, gen)
+        store.calibrate(layer, w["pq_calibration_tokens"])
+        store.assign(layer, 0, S)
+    store.seq_len.fill_(S)
+    q = torch.randn((Ls, B, Hq, D), generator=gen, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    for _ in range(max(args.warmup, 3) + 1):
+        for l in range(Ls):
+            store.decode(l, q[l], scale, top_k, sink, hot, out=out[l])
+    torch.cuda.synchronize()
+    L.device_status()
+    buf = np.zeros(2 * 4096 * 16, dtype=np.uint64)
+    L.check(L.lib().hokv_phase_stamps(buf.ctypes.data_as(ctypes.c_void_p), buf.size), "phase_stamps")
+    st = buf.reshape(2, 4096, 16).astype(np.int64)
+    n6 = min(B * H * 8, 4096)
+    n7 = B * Hq
+    k6 = st[0, :n6, :len(K6_PHASES) + 1]
+    k7 = st[1, :n7, :len(K7_PHASES) + 1]
+    t0 = int(k6[:, 0].min())
+
+    def table(x, names):
+        rows = []
+        for i, name in enumerate(names, start=1):
+            d = (x[:, i] - x[:, i - 1]) / 1e3
+            e = (x[:, i] - t0) / 1e3
+            rows.append({"phase": name, "median_us": float(np.median(d)), "max_us": float(d.max()),
+                         "ends_at_median_us": float(np.median(e)), "ends_at_max_us": float(e.max())})
+        return rows
+
+    line = {"metric": "phase stamps (us) of the last layer's decode kernels", "config": config_for(w, 1),
+            "k6_ctas": n6, "k6_start_spread_us": float((k6[:, 0].max() - t0) / 1e3), "k6": table(k6, K6_PHASES),
+            "k7_ctas": n7, "k7_start_median_us": float(np.median((k7[:, 0] - t0) / 1e3)),
+            "k7_start_max_us": float((k7[:, 0].max() - t0) / 1e3), "k7": table(k7, K7_PHASES),
+            "layer_end_us": float((max(k6[:, -1].max(), k7[:, -1].max()) - t0) / 1e3)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -577,7 +644,12 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="layers to run (default: the workload's 31); fewer only for profiler captures, "
                          "whose JSON line is then not the workload's")
+    ap.add_argument("--phase-stamps", action="store_true",
+                    help="run one step with the profiling build (libhokv_stamps.so) and print per-phase times")
     args = ap.parse_args()
+    if args.phase_stamps:
+        os.environ["HOKV_LIB_VARIANT"] = "stamps"   # read when the package loads the library
+        return run_phase_stamps(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

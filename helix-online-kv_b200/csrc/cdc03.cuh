@@ -382,6 +382,8 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_nl[GT];
 
   pdl_launch_dependents();
+  const int scta = blockIdx.y * gridDim.x + blockIdx.x;   // phase-stamp slot (profiling build)
+  stamp(0, scta, 0);
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   const int R = (int)cl.num_blocks(), me = (int)cl.block_rank();
@@ -442,6 +444,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
     cp_async_wait_all();
     __syncthreads();
+    stamp(0, scta, 1);   // codebook rows and queries staged
     if (staged && p.slots > first) {
       bool more = false;   // the same in every thread: the counts are in shared memory
       for (int sx = s_begin; sx < s_end; ++sx) more |= s_k[sx] > first;
@@ -474,6 +477,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
     }
     __syncthreads();
+    stamp(0, scta, 2);   // dots done
     cluster_wait();             // phase A: every CTA of the cluster runs
     if (tid < GT * 32) {        // own ranges into every CTA
       const int g = tid / 32, sx = tid % 32;
@@ -490,6 +494,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     if (tid < GT) s_cnt[tid] = 0;
     cluster_arrive();
     cluster_wait();             // phase B: all ranges in every CTA
+    stamp(0, scta, 3);   // ranges exchanged
     if (tid < GT) {
       const QuantScale qs = quant_scale(f_lo[tid], f_hi[tid], M, p.scale);
       s_inv[tid] = qs.inv;
@@ -526,6 +531,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         if (own == me) put_entry<CS, GT>(gimg, sx, j, code);
       }
     }
+    stamp(0, scta, 4);   // own image entries written
     cluster_arrive();           // phase C: the image is complete in memory
 #pragma unroll
     for (int it = 0; it < HT; ++it) {   // first codes of the first chunk meanwhile
@@ -537,9 +543,11 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       }
     }
     cluster_wait();
+    stamp(0, scta, 5);   // every CTA's image entries written
     for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
     cp_async_wait_all();
     __syncthreads();
+    stamp(0, scta, 6);   // image in shared memory
   }
 
   // ---- quantised scores of one chunk, kept in registers ----------------------
@@ -701,7 +709,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
 
   // ---- histograms of every own chunk, pooled; threshold ----------------------
   for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
+  stamp(0, scta, 7);   // own chunks scored (thread 0)
   pool_cluster<GT * HWORDS>(hist, full, R, me);
+  stamp(0, scta, 8);   // histograms pooled
   if (warp < GT) {
     const int g = warp;
     const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
@@ -709,6 +719,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
   __syncthreads();
+  stamp(0, scta, 9);   // threshold known
 
   // ---- candidates: the last scored chunk from registers, the others scored again
   emit_chunk(me + (n_mine - 1) * R);
@@ -716,6 +727,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     score_chunk(me + i * R, false, false);
     emit_chunk(me + i * R);
   }
+  stamp(0, scta, 10);  // candidates listed and rescored
 }
 
 template <int D, typename KVT>
@@ -896,6 +908,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int sel_cap = max(p.top_k, p.sink);   // sinks are kept even when top_k < sink_tokens
   const int64_t sel_base = ((int64_t)b * Hq + hq) * sel_cap;
 
+  stamp(1, blockIdx.x, 0);
   for (int d = tid; d < D; d += K7_THREADS)
     s_q[d] = load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)hq * D + d);
   if (tid == 0) s_n = 0;
@@ -911,8 +924,10 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int n_hot = cr.S - cr.Sc;
   at.run(kb, vb, n_hot, warp, scale, [&](int i) { return cr.Sc + i; }, [](int, float) {});
 
+  stamp(1, blockIdx.x, 1);   // hot window attended (thread 0)
   // ---- wait for the candidate stage ------------------------------------------
   pdl_wait();
+  stamp(1, blockIdx.x, 2);   // candidate stage complete
 
   int n_sel;
   bool explicit_sel = false;
@@ -1157,6 +1172,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     n_sel = cr.sink + min(s_n, cr.kp);
     __syncthreads();
   }
+  stamp(1, blockIdx.x, 3);   // selection done
 
   // ---- exact attention over the selected cold tokens, rows straight from
   // memory (16 rows in flight per warp: one round trip for 128 rows)
@@ -1164,6 +1180,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     if (want_scores && at.sl == 0 && i < sel_cap) p.sel_score[sel_base + i] = s;
   });
 
+  stamp(1, blockIdx.x, 4);   // selected tokens attended (thread 0)
   // combine the SUB token groups of this warp, then the warps
 #pragma unroll
   for (int o = A::LPT; o < 32; o <<= 1) {
@@ -1212,6 +1229,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
     }
   }
   if (p.sel_count && tid == 0) p.sel_count[(int64_t)b * Hq + hq] = n_sel;
+  stamp(1, blockIdx.x, 5);
 }
 
 // ---------------------------------------------------------------------------

@@ -609,6 +609,19 @@ int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream) {
   return hokv_cdc03_decode(&b, stream);
 }
 
+int hokv_phase_stamps(uint64_t* out, size_t n_values) {
+#ifdef HOKV_STAMPS
+  const size_t all = (size_t)2 * STAMP_CTAS * STAMP_N;
+  HOKV_REQUIRE(out && n_values >= all, "phase_stamps: need %zu values", all);
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_stamps, all * sizeof(uint64_t));
+  if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "phase_stamps: %s", cudaGetErrorString(e));
+  return HOKV_OK;
+#else
+  (void)out; (void)n_values;
+  return fail(HOKV_ERR_UNSUPPORTED, "phase_stamps: this library was built without -DHOKV_STAMPS");
+#endif
+}
+
 int hokv_dense_attention(const float* q, const float* K, const float* V, int head_dim, int64_t seq_len, int mul_f64,
                          double scale, int store_flags, const uint8_t* mask, void* scores, void* out, void* workspace,
                          size_t workspace_bytes, void* stream) {

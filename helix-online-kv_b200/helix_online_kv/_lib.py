@@ -21,7 +21,10 @@ except ImportError:  # pragma: no cover - torch is a hard dependency of the devi
     torch = None
     _HAS_TORCH = False
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libhokv.so")
+# HOKV_LIB_VARIANT=stamps loads the profiling build (phase stamps in the decode
+# kernels, hokv_phase_stamps); the default is the product library.
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib",
+                        "libhokv_stamps.so" if os.environ.get("HOKV_LIB_VARIANT") == "stamps" else "libhokv.so")
 
 F32, F16, BF16, U8, I32, F64 = 0, 1, 2, 3, 4, 5
 DOT_SEQ_FMA, DOT_GEMV, DOT_L16_PAIR = 0, 1, 2
@@ -102,6 +105,7 @@ _SIGS = {
     "hokv_softmax": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _c_sz, _vp]),
     "hokv_prefilter_mask": (_c_int, [_vp, _c_int, _vp, _c_i64, _c_int, _vp, _vp]),
     "hokv_scale_f32_to_f64": (_c_int, [_vp, _c_i64, _c_f64, _vp, _vp]),
+    "hokv_phase_stamps": (_c_int, [_vp, _c_sz]),
 }
 
 _lock = threading.Lock()

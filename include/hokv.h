@@ -293,6 +293,17 @@ int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream);
 int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* cold_to,
                     int dot_order, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Profiling.  No counterpart in the reference.  A library built with
+ * -DHOKV_STAMPS records, in the two decode kernels, the %globaltimer value
+ * (ns) at each phase boundary, thread 0 of every CTA: out[k][cta][phase] for
+ * kernel k (0: candidate stage, cta = blockIdx.y * gridDim.x + blockIdx.x;
+ * 1: attention stage, cta = blockIdx.x), 4096 CTAs x 16 phases each, the
+ * last launch's values.  n_values must be at least 2 * 4096 * 16.  The
+ * product build returns HOKV_ERR_UNSUPPORTED.
+ * ---------------------------------------------------------------------- */
+int hokv_phase_stamps(uint64_t* out, size_t n_values);
+
 #ifdef __cplusplus
 }
 #endif
