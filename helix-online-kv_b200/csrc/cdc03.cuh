@@ -1,17 +1,20 @@
 // cdc03.cuh -- PQ lookup tables, ADC scoring and CDC-03 decode attention.
 //
-// Decode step, per layer, two kernels chained with programmatic dependent
-// launch (K7 starts its hot-window attention while K6 runs):
+// Decode step, per layer, three kernels chained with programmatic dependent
+// launch (K6 prefetches its codes while K5 runs; K7 starts its hot-window
+// attention while K6 runs):
+//   K5 k5_tables  grid (B*H_kv), one CTA per (sequence, KV head): the exact
+//      fp32 sub-tables T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads
+//      of the GQA group (BLAS order) and their quantised image (codes of
+//      floor(65535 / M) levels in 16-bit lanes, laid out so every
+//      shared-memory lookup of K6 is bank-conflict free).
 //   K6 k6_candidates  grid (min(chunks, 8), B*H_kv), one thread-block cluster
-//      per (sequence, KV head): the CTAs build the exact fp32 sub-tables
-//      T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads of the GQA
-//      group (BLAS order) and their quantised image (codes of floor(65535 / M)
-//      levels in 16-bit lanes, laid out so every shared-memory lookup is bank
-//      conflict free); each CTA streams the uint8 PQ codes of its 2048-token
-//      chunks into registers, sums quantised entries per token in integer
-//      lanes, pools a score histogram over the cluster, and emits every token
-//      whose score lies within the proven error band of the unit's k'-th
-//      score, rescored exactly (reference summation order) into a selection key.
+//      per (sequence, KV head): each CTA copies the image into shared memory,
+//      streams the uint8 PQ codes of its 2048-token chunks into registers,
+//      sums quantised entries per token in integer lanes, pools a score
+//      histogram over the cluster, and emits every token whose score lies
+//      within the proven error band of the unit's k'-th score, rescored
+//      exactly (reference summation order) into a selection key.
 //   K7 k7_select_attend  grid (B*H_kv*G): attends the hot window before it
 //      waits for K6, selects sinks + top-(k - sinks) of the candidate keys
 //      (ties to the lower token index) and finishes softmax attention over them.
@@ -27,7 +30,6 @@
 namespace hokv {
 
 constexpr int K6_THREADS = 256;
-constexpr int K6_FIRST_ROWS = 128;  // codebook rows per subspace staged before the live counts are read
 
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
@@ -55,7 +57,7 @@ struct Cdc03P {
   uint64_t* cand_key;     // [units][chunks][GT][CAND_MAX] selection keys of listed candidates (K6 -> K7)
   int* cand_cnt;          // [units][chunks][GT]   listed count, -1 when the list overflowed
   unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (exchanged in the cluster)
-  float* texact;          // [units][GT][CS][256]    exact sub-tables (K6 rescoring, K7 rescans)
+  float* texact;          // [units][GT][256][CS]    exact sub-tables (K6 rescoring, K7 rescans)
   int* margin;            // [units][GT]             error band in code units
   int n_chunks, chunk, GT, qimg_bytes;
 };
@@ -204,10 +206,8 @@ __device__ __forceinline__ uint16_t quant_code(float t, float lo, float inv, int
 // ===========================================================================
 // K6: candidate stream, grid (min(chunks, 8), B*H_kv), 256 threads, 8 tokens
 // of a 2048-token chunk per thread.  The CTAs of one (b, KV head) form a
-// thread-block cluster that builds the unit's tables itself (each CTA one
-// block of subspaces; ranges exchanged through distributed shared memory, the
-// quantised image through L2) and pools its score histograms, so the
-// threshold is the unit-wide k'-th score at any context length.
+// thread-block cluster that pools its score histograms, so the threshold is
+// the unit-wide k'-th score at any context length; the tables come from K5.
 // ===========================================================================
 constexpr int K6_TPT = 8;
 constexpr int K6_CHUNK = K6_THREADS * K6_TPT;   // 2048 tokens
@@ -306,42 +306,25 @@ __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane)
 template <int CS, int GT>
 constexpr int k6_min_blocks() { return ((GT == 8 && CS >= 16) || (CS == 32 && GT >= 4)) ? 3 : 4; }
 
-// Dot phase of the in-cluster table build: thread j computes entry j of the
-// subspaces [s_begin, s_end) for the GT query heads of the group, stores the
-// exact fp32 value (for the exact rescoring), folds it into the
-// per-(head, subspace) range and keeps the first two subspaces' values in
-// registers for the quantisation.  Row (s, j) of the codebook is at
-// rows + ((s - s_off) * slots + j) * SD.
-template <int GT, int SD>
-__device__ __forceinline__ void lut_dot_row(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
-                                            const int* s_k, int s, unsigned (*s_lo)[32], unsigned (*s_hi)[32],
-                                            float (&tv)[GT]) {
-  const int j = threadIdx.x, lane = j & 31;
-  const bool live = j < s_k[s];
-  float c[SD];
-  const float* row = rows + ((int64_t)(s - s_off) * p.slots + j) * SD;
+// Exact sub-table entry T = q . c for one codebook row: the reference GEMV
+// order (hokv_math.cuh dot_gemv) with the paired products and sums of the
+// 4- and 8-dim orders in fp32x2 operations, which round each lane as its
+// scalar twin does.
+template <int SD>
+__device__ __forceinline__ float lut_dot2(const float* q, const float* c) {
+  if constexpr (SD == 4) {
+    const float2 a = __fmul2_rn(make_float2(q[0], q[2]), make_float2(c[0], c[2]));
+    const float2 b = __fmul2_rn(make_float2(q[1], q[3]), make_float2(c[1], c[3]));
+    const float2 s = __fadd2_rn(a, b);   // {p0 + p1, p2 + p3}
+    return fadd(s.x, s.y);
+  } else if constexpr (SD == 8) {
+    float2 pr[4];
 #pragma unroll
-  for (int d = 0; d < SD; ++d) c[d] = live ? row[d] : 0.f;
-#pragma unroll
-  for (int g = 0; g < GT; ++g) {
-    const float t = live ? lut_dot<SD>(sq + g * p.D + s * SD, c) : 0.f;
-    tv[g] = t;
-    p.texact[(((int64_t)u * GT + g) * p.CS + s) * 256 + j] = t;
-    const unsigned o = ord_f32(t);
-    const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
-    if (lane == 0) { atomicMin(&s_lo[g][s], mn); atomicMax(&s_hi[g][s], mx); }
-  }
-}
-
-template <int GT, int SD>
-__device__ __forceinline__ void lut_dots(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
-                                         const int* s_k, int s_begin, int s_end, unsigned (*s_lo)[32],
-                                         unsigned (*s_hi)[32], float (&tv)[2][GT]) {
-  if (s_begin < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin, s_lo, s_hi, tv[0]);
-  if (s_begin + 1 < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin + 1, s_lo, s_hi, tv[1]);
-  for (int s = s_begin + 2; s < s_end; ++s) {
-    float tmp[GT];
-    lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s, s_lo, s_hi, tmp);
+    for (int i = 0; i < 4; ++i) pr[i] = __fmul2_rn(make_float2(q[i], q[i + 4]), make_float2(c[i], c[i + 4]));
+    const float2 s = __fadd2_rn(__fadd2_rn(pr[0], pr[1]), __fadd2_rn(pr[2], pr[3]));
+    return fadd(s.x, s.y);   // ((p0+p1)+(p2+p3)) + ((p4+p5)+(p6+p7))
+  } else {
+    return dot_gemv(q, c, SD);
   }
 }
 
@@ -365,6 +348,153 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
     if constexpr (Q::EW == 4) reinterpret_cast<uint32_t*>(img)[e] = e32[0];
     else if constexpr (Q::EW == 8) reinterpret_cast<uint2*>(img)[e] = make_uint2(e32[0], e32[1]);
     else reinterpret_cast<uint4*>(img)[e] = make_uint4(e32[0], e32[1], e32[2], e32[3]);
+  }
+}
+
+// ===========================================================================
+// K5: the unit's sub-tables and their quantised image, one CTA per
+// (sequence, KV head), K5_THREADS threads.  Thread t takes subspace column
+// s = t % CS and the rows j = t / CS + i * (K5_THREADS / CS) of that column;
+// it loads its live codebook rows straight into registers (every load in
+// flight at once), computes each entry T[g][s][j] = q_g[s] . C_s[j] exactly
+// (reference GEMV order) and stores it into texact[u][g][j][s] (the exact
+// rescoring of k6 and k7 reads it); the per-(head, subspace) ranges are reduced by
+// shuffles and shared atomics, each head gets one quantisation step and error
+// band (quant_scale; the band goes to `margin`), and every quantised entry is
+// written into the unit's image in global memory, which k6 copies into shared
+// memory.  Rows at or past a subspace's live count have the entry 0, padding
+// columns [M, CS) the code 0.
+// ===========================================================================
+constexpr int K5_THREADS = 512;
+
+template <int CS, int GT, int SD>
+__device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, float* sq) {
+  constexpr int TPS = K5_THREADS / CS;   // threads per column
+  constexpr int NS = 256 / TPS;          // row slots per thread
+  __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
+  __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int s = tid % CS, r0 = tid / CS;
+  const int M = p.M;
+  const float* col = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh + (int64_t)(s < M ? s : 0) * p.slots * SD;
+  int ks = 0;
+  if (s < M) {
+    ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
+    ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
+  }
+  // rows in registers NB at a time (all of them for sub_dim <= 8)
+  constexpr int NB = (SD <= 8) ? NS : ((64 / SD) < 1 ? 1 : (64 / SD) > NS ? NS : (64 / SD));
+  auto load_rows = [&](int i0, float (&c)[NB][SD]) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      const int j = r0 + (i0 + i) * TPS;
+      if (i0 + i < NS && j < ks) {
+#pragma unroll
+        for (int d = 0; d < SD; d += 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(col + (int64_t)j * SD + d));
+          c[i][d] = v.x; c[i][d + 1] = v.y; c[i][d + 2] = v.z; c[i][d + 3] = v.w;
+        }
+      }
+    }
+  };
+  float c[NB][SD];
+  load_rows(0, c);
+  for (int i = tid; i < GT * p.D; i += K5_THREADS) {
+    const int g = i / p.D, d = i - g * p.D;
+    sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
+  }
+  if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
+  __syncthreads();
+  stamp(2, blockIdx.x, 1);   // queries staged
+  float e[NS][GT];
+  unsigned lo[GT], hi[GT];
+#pragma unroll
+  for (int g = 0; g < GT; ++g) { lo[g] = 0xffffffffu; hi[g] = 0u; }
+  const int64_t tx = (int64_t)u * GT * CS * 256;
+#pragma unroll
+  for (int i0 = 0; i0 < NS; i0 += NB) {
+    if (i0 > 0) load_rows(i0, c);
+#pragma unroll
+    for (int g = 0; g < GT; ++g) {
+      float qs[SD];
+#pragma unroll
+      for (int d = 0; d < SD; ++d) qs[d] = s < M ? sq[g * p.D + s * SD + d] : 0.f;
+#pragma unroll
+      for (int i = 0; i < NB; ++i) {
+        if (i0 + i < NS) {
+          const int j = r0 + (i0 + i) * TPS;
+          float v = 0.f;
+          if (j < ks) {
+            v = lut_dot2<SD>(qs, c[i]);
+            const unsigned o = ord_f32(v);
+            lo[g] = min(lo[g], o);
+            hi[g] = max(hi[g], o);
+          }
+          e[i0 + i][g] = v;
+          if (s < M) p.texact[tx + ((int64_t)g * 256 + j) * CS + s] = v;
+        }
+      }
+    }
+  }
+  // ranges of each (head, column): lanes of one column, then the warps
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+#pragma unroll
+    for (int o = CS; o < 32; o <<= 1) {
+      lo[g] = min(lo[g], __shfl_xor_sync(0xffffffffu, lo[g], o));
+      hi[g] = max(hi[g], __shfl_xor_sync(0xffffffffu, hi[g], o));
+    }
+    if (lane < CS && s < M) { atomicMin(&s_lo[g][s], lo[g]); atomicMax(&s_hi[g][s], hi[g]); }
+  }
+  __syncthreads();
+  stamp(2, blockIdx.x, 2);   // entries and ranges
+  if (tid < GT * 32) {
+    const int g = tid / 32, sx = tid % 32;
+    if (sx < M) {
+      int kx = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + sx];
+      kx = kx < 0 ? 0 : (kx > p.slots ? p.slots : kx);
+      unsigned ol = s_lo[g][sx], oh = s_hi[g][sx];
+      if (kx < 256) { ol = min(ol, ord_f32(0.f)); oh = max(oh, ord_f32(0.f)); }   // zero entries of dead rows
+      float fl = unord_f32(ol), fh = unord_f32(oh);
+      if (kx < 256) { fl = fminf(fl, 0.f); fh = fmaxf(fh, 0.f); }
+      f_lo[g][sx] = fl;
+      f_hi[g][sx] = fh;
+    }
+  }
+  __syncthreads();
+  if (tid < GT) {
+    const QuantScale qsc = quant_scale(f_lo[tid], f_hi[tid], M, p.scale);
+    s_inv[tid] = qsc.inv;
+    p.margin[(int64_t)u * GT + tid] = qsc.margin;
+  }
+  __syncthreads();
+  unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
+  const int qmax = qmax_for(M);
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    uint32_t code[GT];
+#pragma unroll
+    for (int g = 0; g < GT; ++g) code[g] = (s < M) ? quant_code(e[i][g], f_lo[g][s], s_inv[g], qmax) : 0u;
+    put_entry<CS, GT>(gimg, s, r0 + i * TPS, code);
+  }
+  stamp(2, blockIdx.x, 3);   // image stored
+}
+
+template <int CS, int GT>
+__global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
+  extern __shared__ __align__(16) float k5_sq[];   // [GT][D] queries
+  pdl_launch_dependents();   // k6 may start: it prefetches its codes, then waits for this grid
+  stamp(2, blockIdx.x, 0);
+  const int u = blockIdx.x;
+  const int b = u / p.Hkv, h = u - b * p.Hkv;
+  const ColdRange cr = cold_range(p, b);
+  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking: k6 and k7 read no table
+  switch (p.sd) {
+    case 4: k5_body<CS, GT, 4>(p, u, b, h, k5_sq); break;
+    case 8: k5_body<CS, GT, 8>(p, u, b, h, k5_sq); break;
+    case 16: k5_body<CS, GT, 16>(p, u, b, h, k5_sq); break;
+    case 32: k5_body<CS, GT, 32>(p, u, b, h, k5_sq); break;
+    default: dev_flag(HOKV_ERR_DEVICE_INPUT);
   }
 }
 
@@ -403,138 +533,16 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   uint32_t w[HT][Q::W];
   const int c0 = me;
   {
-    // ---- tables built by the cluster: each CTA computes a block of subspaces
-    // (whole 16-byte groups of the image), the ranges go to every CTA through
-    // distributed shared memory, the quantised entries to the unit's image in
-    // global memory, from where every CTA loads the whole image
-    __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
-    __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
-    __shared__ int s_k[32];
-    cluster_arrive_relaxed();   // phase A: this CTA runs
-    constexpr int GS = 16 / Q::EW;                 // subspaces per 16-byte group
-    const int ngm = (M + GS - 1) / GS;             // groups holding real subspaces
-    const int grp0 = me * ngm / R, grp1 = (me + 1) * ngm / R;
-    const int s_begin = grp0 * GS, s_end = min(grp1 * GS, M);
-    const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-    // own codebook rows into shared memory (the image space is free until the
-    // image is loaded), with the queries: the first K6_FIRST_ROWS rows of each
-    // subspace now, the live rows past them (if any) once the counts are known
-    const int64_t per_s = (int64_t)p.slots * p.sd;                           // floats per subspace
-    const int64_t blk = (int64_t)max(0, s_end - s_begin) * per_s;
-    const bool staged = blk * 4 <= Q::BYTES;
-    const float* src = cbase + (int64_t)s_begin * per_s;
-    const int first = min(p.slots, K6_FIRST_ROWS);
-    const int row16 = p.sd / 4;                                              // 16-byte pieces per row
-    if (staged) {
-      const int64_t n16 = (int64_t)(s_end - s_begin) * first * row16;
-      for (int64_t i = tid; i < n16; i += K6_THREADS) {
-        const int64_t sr = i / (first * row16), off = sr * per_s + (i - sr * first * row16) * 4;
-        cp_async16(qlut + off * 4, src + off);
-      }
-    }
-    float* sq = reinterpret_cast<float*>(hist);   // [GT][D], dead before the histograms
-    for (int i = tid; i < GT * p.D; i += K6_THREADS) {
-      const int g = i / p.D, d = i - g * p.D;
-      sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
-    }
-    if (tid < M) {
-      const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
-      s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-    }
-    if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
-    cp_async_wait_all();
-    __syncthreads();
-    stamp(0, scta, 1);   // codebook rows and queries staged
-    if (staged && p.slots > first) {
-      bool more = false;   // the same in every thread: the counts are in shared memory
-      for (int sx = s_begin; sx < s_end; ++sx) more |= s_k[sx] > first;
-      if (more) {
-        for (int sx = s_begin; sx < s_end; ++sx) {
-          const int64_t base = (int64_t)(sx - s_begin) * per_s + (int64_t)first * p.sd;
-          const int64_t n16 = (int64_t)max(0, s_k[sx] - first) * row16;
-          for (int64_t i = tid; i < n16; i += K6_THREADS) cp_async16(qlut + (base + i * 4) * 4, src + base + i * 4);
-        }
-        cp_async_wait_all();
-        __syncthreads();
-      }
-    }
-    float tv[2][GT];
-    const float* rows = staged ? reinterpret_cast<const float*>(qlut) : cbase;
-    const int s_off = staged ? s_begin : 0;
-    switch (p.sd) {
-      case 4: lut_dots<GT, 4>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
-      case 8: lut_dots<GT, 8>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
-      case 16: lut_dots<GT, 16>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
-      case 32: lut_dots<GT, 32>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
-      default: dev_flag(HOKV_ERR_DEVICE_INPUT);
-    }
-    // this CTA's codes into L2 while the cluster exchanges and quantises the
-    // tables (issued after the table reads, which are on the critical path)
+    // ---- codes of this CTA into L2 and its first half-chunk into registers,
+    // then the unit's tables from k5 (programmatic launch: k5 may still run)
     for (int i = 0; i < n_mine; ++i) {
       const int t0 = (me + i * R) * K6_CHUNK;
       const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
       for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
     }
-    __syncthreads();
-    stamp(0, scta, 2);   // dots done
-    cluster_wait();             // phase A: every CTA of the cluster runs
-    if (tid < GT * 32) {        // own ranges into every CTA
-      const int g = tid / 32, sx = tid % 32;
-      if (sx >= s_begin && sx < s_end) {
-        float lo = unord_f32(s_lo[g][sx]), hi = unord_f32(s_hi[g][sx]);
-        if (s_k[sx] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
-        for (int rk = 0; rk < R; ++rk) {
-          cl.map_shared_rank(&f_lo[0][0], (unsigned)rk)[g * 32 + sx] = lo;
-          cl.map_shared_rank(&f_hi[0][0], (unsigned)rk)[g * 32 + sx] = hi;
-        }
-      }
-    }
-    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
-    if (tid < GT) s_cnt[tid] = 0;
-    cluster_arrive();
-    cluster_wait();             // phase B: all ranges in every CTA
-    stamp(0, scta, 3);   // ranges exchanged
-    if (tid < GT) {
-      const QuantScale qs = quant_scale(f_lo[tid], f_hi[tid], M, p.scale);
-      s_inv[tid] = qs.inv;
-      s_margin[tid] = qs.margin;
-      if (me == 0) p.margin[(int64_t)u * GT + tid] = qs.margin;
-    }
-    __syncthreads();
-    unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-    {
-      const int qmax = qmax_for(M), j = tid;
-      uint32_t code[GT];
 #pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const int sx = s_begin + kk;
-        if (sx < s_end) {
-#pragma unroll
-          for (int g = 0; g < GT; ++g) code[g] = quant_code(tv[kk][g], f_lo[g][sx], s_inv[g], qmax);
-          put_entry<CS, GT>(gimg, sx, j, code);
-        }
-      }
-      for (int sx = s_begin + 2; sx < s_end; ++sx) {
-#pragma unroll
-        for (int g = 0; g < GT; ++g)
-          code[g] = quant_code(p.texact[(((int64_t)u * GT + g) * CS + sx) * 256 + j], f_lo[g][sx], s_inv[g], qmax);
-        put_entry<CS, GT>(gimg, sx, j, code);
-      }
-      // padding subspaces [M, CS): zero entries, written by the owner of the
-      // group (rank 0 for groups without a real subspace)
-#pragma unroll
-      for (int g = 0; g < GT; ++g) code[g] = 0u;
-      for (int sx = M; sx < CS; ++sx) {
-        const int grp = sx / GS;
-        const int own = grp < ngm ? ((grp + 1) * R - 1) / ngm : 0;
-        if (own == me) put_entry<CS, GT>(gimg, sx, j, code);
-      }
-    }
-    stamp(0, scta, 4);   // own image entries written
-    cluster_arrive();           // phase C: the image is complete in memory
-#pragma unroll
-    for (int it = 0; it < HT; ++it) {   // first codes of the first chunk meanwhile
+    for (int it = 0; it < HT; ++it) {
       const int t = c0 * K6_CHUNK + it * K6_THREADS + tid;
       if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
       else {
@@ -542,12 +550,15 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
       }
     }
-    cluster_wait();
-    stamp(0, scta, 5);   // every CTA's image entries written
+    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
+    if (tid < GT) s_cnt[tid] = 0;
+    pdl_wait();   // k5 complete: image, exact sub-tables and error bands in memory
+    const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
     for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
+    if (tid < GT) s_margin[tid] = __ldcg(p.margin + (int64_t)u * GT + tid);
     cp_async_wait_all();
     __syncthreads();
-    stamp(0, scta, 6);   // image in shared memory
+    stamp(0, scta, 1);   // image in shared memory
   }
 
   // ---- quantised scores of one chunk, kept in registers ----------------------
@@ -689,10 +700,10 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       const uint32_t t = list[g * CAND_MAX + slot];
       uint32_t cw[Q::W];
       load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
-      const float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
+      const float* tex = p.texact + ((int64_t)u * GT + g) * 256 * CS;
       float e[CS];
 #pragma unroll
-      for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + s * 256 + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu)) : 0.f;
+      for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu) * CS + s) : 0.f;
       float sum = 0.f;   // reference order: ((0 + T0[c0]) + T1[c1]) + ...
 #pragma unroll
       for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
@@ -709,9 +720,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
 
   // ---- histograms of every own chunk, pooled; threshold ----------------------
   for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
-  stamp(0, scta, 7);   // own chunks scored (thread 0)
+  stamp(0, scta, 2);   // own chunks scored (thread 0)
   pool_cluster<GT * HWORDS>(hist, full, R, me);
-  stamp(0, scta, 8);   // histograms pooled
+  stamp(0, scta, 3);   // histograms pooled
   if (warp < GT) {
     const int g = warp;
     const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
@@ -719,7 +730,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
   __syncthreads();
-  stamp(0, scta, 9);   // threshold known
+  stamp(0, scta, 4);   // threshold known
 
   // ---- candidates: the last scored chunk from registers, the others scored again
   emit_chunk(me + (n_mine - 1) * R);
@@ -727,7 +738,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     score_chunk(me + i * R, false, false);
     emit_chunk(me + i * R);
   }
-  stamp(0, scta, 10);  // candidates listed and rescored
+  stamp(0, scta, 5);   // candidates listed and rescored
 }
 
 template <int D, typename KVT>
@@ -886,8 +897,8 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   using AT = Attn<D, KVT>;
   constexpr int NW = AT::NW;
   extern __shared__ __align__(16) unsigned char smem[];
-  float* T = reinterpret_cast<float*>(smem);                                 // [M][256] exact sub-table
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.M * 1024);           // [K7_CAP]
+  float* T = reinterpret_cast<float*>(smem);                                 // [256][CS] exact sub-table
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.CS * 1024);          // [K7_CAP]
   uint32_t* hist = reinterpret_cast<uint32_t*>(keys + K7_CAP);               // [256]
   int* sel = reinterpret_cast<int*>(hist + 256);                             // [TOPK_MAX]
   float* part = reinterpret_cast<float*>(sel + TOPK_MAX);                    // [NW][D + 2]
@@ -1004,8 +1015,8 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
       }
       __syncthreads();
       if (s_over) {   // exact sub-table of this head, for the rescan of overflowed chunks
-        const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
-        for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
+        const float* tex = p.texact + ((int64_t)u * p.GT + g) * 256 * p.CS;
+        for (int i = tid; i < p.CS * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
       }
       const int n_listed = s_off[p.n_chunks];
       for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
@@ -1071,7 +1082,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   #pragma unroll
                 for (int w = 0; w < 8; ++w) cw[w] = (w < p.CS / 4) ? __ldg(row + w) : 0u;   // one row, loads in flight together
                 float sum = 0.f;
-                for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[s2 * 256 + ((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu)]);
+                for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu) * p.CS + s2]);
                 fn(sel_key(fmul(sum, scale), (uint32_t)t), n_listed + s_ooff[c] + (t - clo));
               }
             }

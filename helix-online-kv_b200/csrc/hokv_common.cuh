@@ -62,12 +62,13 @@ __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 
 // ---- phase stamps (profiling build only) ----------------------------------
 // Built with -DHOKV_STAMPS, the decode kernels record %globaltimer at their
-// phase boundaries (thread 0 of each CTA) into g_stamps[kernel][cta][phase];
+// phase boundaries (thread 0 of each CTA) into g_stamps[kernel][cta][phase]
+// (kernel 0: candidate stream, 1: attention, 2: tables);
 // hokv_phase_stamps() copies them out.  The product build compiles no stamp.
 constexpr int STAMP_CTAS = 4096;
 constexpr int STAMP_N = 16;
 #ifdef HOKV_STAMPS
-__device__ unsigned long long g_stamps[2][STAMP_CTAS][STAMP_N];
+__device__ unsigned long long g_stamps[3][STAMP_CTAS][STAMP_N];
 __device__ __forceinline__ void stamp(int kernel, int cta, int phase) {
   if (threadIdx.x == 0 && cta < STAMP_CTAS) {
     unsigned long long t;

@@ -8,6 +8,7 @@
 #include "cdc03.cuh"
 #include "codec.cuh"
 #include "dense.cuh"
+#include "assign_tc.cuh"
 
 #include <map>
 #include <mutex>
@@ -96,20 +97,24 @@ static int launch_ex(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st
   return check_launch(what);
 }
 
-// Stage 1: K5 (tables, ordinary launch: it reads the queries) then K6
-// (candidates, programmatic launch: it prefetches its codes while K5 runs).
-// Stage 1: one thread-block cluster of min(chunks, K6_CLUSTER_MAX) CTAs per
-// unit builds the tables and streams the candidates (ordinary launch: it
-// reads the queries).
+// Stage 1: K5 (tables, one CTA per unit, ordinary launch: it reads the
+// queries) then K6 (candidates, one thread-block cluster of
+// min(chunks, K6_CLUSTER_MAX) CTAs per unit, programmatic launch: it prefetches
+// its codes while K5 runs and waits for K5 before it reads the image).
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
+  const size_t sm5 = (size_t)GT * p.D * 4;   // queries
+  if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
+  if (int e = launch_ex(k5_tables<CS, GT>, dim3((unsigned)(p.B * p.Hkv)), dim3(K5_THREADS), sm5, st, p,
+                        "k5_tables", false))
+    return e;
   const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
   const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
   if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
   return launch_ex(k6_candidates<CS, GT>, dim3((unsigned)R, (unsigned)(p.B * p.Hkv)), dim3(K6_THREADS), sm, st, p,
-                   "k6_candidates", false, R);
+                   "k6_candidates", true, R);
 }
 
 static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
@@ -132,7 +137,7 @@ static int qimg_bytes_for(int CS, int GT) {
 // Stage 2: K7, programmatic launch (hot-window attention overlaps K6).
 template <int D, typename KVT>
 static int launch_k7(const Cdc03P& p, cudaStream_t st) {
-  const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
+  const size_t sm = (size_t)p.CS * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
                     (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)K7_KEYCACHE_BYTES;
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
   return launch_ex(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
@@ -309,6 +314,46 @@ int hokv_scalar_vq_qkt(const float* q, const void* idx, int idx_dtype, int64_t s
 }
 
 // ------------------------------------------------------------ vector / PQ ---
+}  // extern "C"
+
+namespace hokv {
+template <int SD>
+static int launch_assign_tc_sd(const void* x, int x_dtype, int64_t n, int64_t xrs, int64_t xss, int M,
+                               const float* cents, int slots, int64_t css, const int* k, int64_t kss, uint8_t* out,
+                               int64_t ors, int64_t oss, int n_sets, cudaStream_t st) {
+  constexpr int KX = (SD + 7) / 8, KL = 8 * KX, KE = KL + 8, KA = 2 * KL + 8;
+  size_t sm = (size_t)TC_ROWS * KA * 4 + (size_t)256 * KE * 4 + (size_t)256 * KL * 4 + 256 * 4 + 64;
+  // at most two CTAs per SM: each holds TC_TMEM_COLS of the 512 tensor-memory columns
+  sm = std::max<size_t>(sm, 80 * 1024);
+  if (int e = ensure_smem(k_pq_assign_tc<SD>, sm)) return e;
+  int dev = 0, n_sm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n_tiles = cdiv(n, TC_ROWS);
+  const int64_t units = (int64_t)M * n_sets;
+  // about four tiles per CTA (the staged codebook is reused), at least two CTAs per SM
+  int64_t groups = std::max<int64_t>(cdiv(n_tiles, 4), cdiv(2 * n_sm, units));
+  groups = std::min<int64_t>(std::min<int64_t>(groups, n_tiles), 65535);
+  k_pq_assign_tc<SD><<<dim3((unsigned)M, (unsigned)groups, (unsigned)n_sets), TC_THREADS, sm, st>>>(
+      x, x_dtype, n, xrs, xss, cents, slots, css, k, kss, out, ors, oss);
+  return check_launch("k_pq_assign_tc");
+}
+
+static int launch_assign_tc(const void* x, int x_dtype, int64_t n, int64_t xrs, int64_t xss, int M, int sd,
+                            const float* cents, int slots, int64_t css, const int* k, int64_t kss, uint8_t* out,
+                            int64_t ors, int64_t oss, int n_sets, cudaStream_t st) {
+#define HOKV_TC(sd_)                                                                                       \
+  if (sd == sd_)                                                                                          \
+    return launch_assign_tc_sd<sd_>(x, x_dtype, n, xrs, xss, M, cents, slots, css, k, kss, out, ors, oss, \
+                                    n_sets, st);
+  HOKV_TC(4) HOKV_TC(8) HOKV_TC(16) HOKV_TC(32) HOKV_TC(64)
+#undef HOKV_TC
+  return fail(HOKV_ERR_UNSUPPORTED, "pq_assign: tensor-core path for sub_dim %d", sd);
+}
+}  // namespace hokv
+
+extern "C" {
+
 int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, int64_t x_set_stride, int M,
                    int sub_dim, const float* cents, int cb_slots, int64_t cent_set_stride, const int* k,
                    int64_t k_set_stride, uint8_t* out, int64_t out_row_stride, int64_t out_set_stride, int n_sets,
@@ -320,6 +365,13 @@ int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, 
   HOKV_REQUIRE(x_dtype == HOKV_F32 || x_dtype == HOKV_F16 || x_dtype == HOKV_BF16, "pq_assign: dtype %d", x_dtype);
   HOKV_REQUIRE(sub_dim <= 1024, "pq_assign: sub_dim %d > 1024", sub_dim);
   if (n == 0) return HOKV_OK;
+  if (dot_order == DOT_SEQ_FMA && n >= TC_MIN_ROWS &&
+      (sub_dim == 4 || sub_dim == 8 || sub_dim == 16 || sub_dim == 32 || sub_dim == 64) && M <= 65535 &&
+      n_sets <= 65535) {
+    // prefill-sized batches: tensor-core screen, exact rescoring
+    return launch_assign_tc(x, x_dtype, n, x_row_stride, x_set_stride, M, sub_dim, cents, cb_slots, cent_set_stride,
+                            k, k_set_stride, out, out_row_stride, out_set_stride, n_sets, S(stream));
+  }
   if (dot_order == DOT_SEQ_FMA && (sub_dim == 4 || sub_dim == 8)) {
     // prefill-sized batches: register-tiled kernel, same arithmetic
     HOKV_REQUIRE(cdiv(n, 1024) < (1ll << 31) && M <= 65535 && n_sets <= 65535, "pq_assign: grid too large");
@@ -611,7 +663,7 @@ int hokv_cdc03_decode_noalloc(const hokv_cdc03_args* a, void* stream) {
 
 int hokv_phase_stamps(uint64_t* out, size_t n_values) {
 #ifdef HOKV_STAMPS
-  const size_t all = (size_t)2 * STAMP_CTAS * STAMP_N;
+  const size_t all = (size_t)3 * STAMP_CTAS * STAMP_N;
   HOKV_REQUIRE(out && n_values >= all, "phase_stamps: need %zu values", all);
   cudaError_t e = cudaMemcpyFromSymbol(out, g_stamps, all * sizeof(uint64_t));
   if (e != cudaSuccess) return fail(HOKV_ERR_CUDA, "phase_stamps: %s", cudaGetErrorString(e));

@@ -87,13 +87,13 @@ class CDC03Store:
             return
         if order is None:
             order = L.dot_order_for(n, self.sd)
-        for b in range(self.B):
-            x = self.k[layer, b, :, start:end, :]
-            out = self.codes[layer, b, :, start:end, :]
-            L.check(L.lib().hokv_pq_assign(L.ptr(x), L.dtype_code(x), n, self.D, self.cap * self.D, self.M, self.sd,
-                                           L.ptr(self.codebook[layer, b]), SLOTS, self.M * SLOTS * self.sd,
-                                           L.ptr(self.cb_k[layer, b]), self.M, L.ptr(out), self.CS,
-                                           self.cap * self.CS, self.H, order, L.stream()), "pq_assign")
+        # one launch over every (sequence, head): sets are B * H_kv equally strided tiers
+        x = self.k[layer, :, :, start:end, :]
+        out = self.codes[layer, :, :, start:end, :]
+        L.check(L.lib().hokv_pq_assign(L.ptr(x), L.dtype_code(x), n, self.D, self.cap * self.D, self.M, self.sd,
+                                       L.ptr(self.codebook[layer]), SLOTS, self.M * SLOTS * self.sd,
+                                       L.ptr(self.cb_k[layer]), self.M, L.ptr(out), self.CS,
+                                       self.cap * self.CS, self.B * self.H, order, L.stream()), "pq_assign")
 
     # ---- checkpoint / resume ---------------------------------------------------
     _STATE = ("k", "v", "codes", "codebook", "cb_k", "seq_len")
