@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(TC_THREADS) k_pq_assign_tc(const void* __restr
     phase ^= 1u;
     tc_fence_after();
     // pass 1: the row's largest screen value and each 32-column chunk's
-    const int nch = np >> 5 | ((np & 31) ? 1 : 0);
+    const int nch = (np + 31) >> 5;   // 32-column chunks holding the np MMA columns
     float cmaxs[8];
     float m = -INFINITY;
 #pragma unroll
