@@ -184,3 +184,48 @@ def test_cdc03_attention_in_hf_model():
             assert cos > 0.9999 and (got - ref).abs().max().item() < 5e-2, (cos, (got - ref).abs().max().item())
         else:
             assert cos > 0.9, cos
+
+
+def test_cdc03_cache_keeps_one_copy():
+    """Compressed layers keep their K/V only in the CDC-03 store (their cache
+    layers are views into it): after a 4K-token prefill the cache's device
+    bytes are the dense cache's plus the PQ codes and codebooks (under 15 %
+    more), where a dense copy beside the store doubled them; memory_report
+    counts exactly the allocated tensors; and the decode step with a budget
+    covering the cold range equals the dense cache's."""
+    transformers = pytest.importorskip("transformers")
+    from helix_online_kv.cdc03_attention import CDC03Cache
+    from helix_online_kv.config import OnlineKVConfig
+    cfg = transformers.LlamaConfig(vocab_size=256, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                                   num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=8192)
+    torch.manual_seed(1)
+    model = transformers.LlamaForCausalLM(cfg).cuda().half().eval()
+    model.config._attn_implementation = "sdpa"
+    S = 4096
+    ids = torch.randint(0, 256, (1, S), device="cuda")
+    with torch.no_grad():
+        dense = transformers.DynamicCache()
+        out = model(ids, past_key_values=dense, use_cache=True)
+        nxt = out.logits[:, -1:].argmax(-1)
+        ref = model(nxt, past_key_values=dense, use_cache=True).logits[0, -1].float()
+    dense_bytes = sum(t.element_size() * t.nelement() for layer in dense.layers for t in (layer.keys, layer.values))
+    del out
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    kvc = OnlineKVConfig(calibration_tokens=128, hot_window=256, pq_subspaces=8, exact_layers=[0], top_k=S + 16)
+    cache = CDC03Cache(kvc, n_layers=4, batch=1, kv_heads=2, head_dim=64, capacity=S + 1, dtype=torch.float16)
+    cache.attach(model)
+    with torch.no_grad():
+        model(ids, past_key_values=cache, use_cache=True)
+        torch.cuda.synchronize()
+        held = torch.cuda.memory_allocated() - before
+        got = model(nxt, past_key_values=cache, use_cache=True).logits[0, -1].float()
+    model.config._attn_implementation = "sdpa"
+    rep = cache.memory_report()
+    st = cache.store
+    assert st.k.shape[0] == 3, "the store holds the compressed layers only"
+    assert rep["total_bytes"] <= 1.15 * dense_bytes, (rep, dense_bytes)
+    assert held <= 1.2 * dense_bytes, (held, dense_bytes)
+    assert cache.layers[1].keys.data_ptr() == st.k[0].data_ptr(), "compressed layers are views of the store"
+    cos = torch.nn.functional.cosine_similarity(got, ref, dim=0).item()
+    assert cos > 0.9999 and (got - ref).abs().max().item() < 5e-2
