@@ -392,6 +392,59 @@ def long_context(world, rank, steps, contexts=(32768, 131072)):
     return res
 
 
+def head_sharded(world, rank, steps, S=16384, Ls=31):
+    """One sequence (fewer sequences than GPUs) at the Llama-3-8B KV geometry
+    (8 KV heads, 32 query heads, head_dim 128, PQ 16 x 8) and 16K context,
+    31 layers, its KV heads split over the ranks; after every layer one
+    all-gather of the [1, 32, 128] outputs over NCCL, whose result is the next
+    layer's queries (a stand-in for the model's projections), so that each
+    layer waits for the collective.  Eager launches, device-timed, max over
+    ranks."""
+    import torch
+    from helix_online_kv.cdc03 import CDC03Store
+    from helix_online_kv.sharding import gather_heads, head_shard, max_over_ranks
+    H_all, G, D, M = 8, 4, 128, 16
+    heads = head_shard(H_all, world, rank)
+    H = len(heads)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(99 + rank)
+    store = CDC03Store(1, Ls, max(H, 1), D, S, n_subspaces=M, dtype=torch.bfloat16) if H else None
+    if store is not None:
+        for l in range(Ls):
+            _fill_uniform(store, l, gen, S)
+            store.calibrate(l, 128)
+            store.assign(l, 0, S)
+        store.seq_len.fill_(S)
+    q0 = torch.randn((1, H_all * G, D), generator=gen, device="cuda").to(torch.bfloat16)
+    qs = slice(heads.start * G, heads.stop * G)
+    scale = 1.0 / np.sqrt(D)
+
+    def step():
+        q = q0
+        for l in range(Ls):
+            if store is not None:
+                o = store.decode(l, q[:, qs].contiguous(), scale, 128, 4, 256)
+            else:
+                o = torch.empty((1, 0, D), dtype=q.dtype, device="cuda")
+            q = gather_heads(o, H_all, G)
+        return q
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), device="cuda") / steps
+    return {"geometry": "1 sequence, Llama-3-8B KV, 16K context, 31 layers, KV heads split over the GPUs",
+            "kv_heads_per_gpu": H, "ms_per_step": ms, "tokens_per_s": 1e3 / ms,
+            "collective": "NCCL all-gather of the [1, 32, 128] attention outputs after every layer"
+                          if world > 1 else "none (one GPU)"}
+
+
 def encoder_sweep(ns=(1, 16, 256, 4096, 32768), reps=5):
     """Online encoder sweep: N new fp16 K vectors per step assigned to per-(layer,
     head) k=256 codebooks, 22 layers x 4 KV heads x head_dim 64, for the scalar,
@@ -677,7 +730,8 @@ def run_ours(args):
         graph = api_graph = None
         torch.cuda.empty_cache()
         for name, fn in (("encoder_sweep", lambda: encoder_sweep()),
-                         ("long_context", lambda: long_context(world, rank, max(3, min(args.steps, 10))))):
+                         ("long_context", lambda: long_context(world, rank, max(3, min(args.steps, 10)))),
+                         ("head_sharded_1seq", lambda: head_sharded(world, rank, max(3, min(args.steps, 10))))):
             try:
                 extras[name] = fn()
             except Exception as e:   # noqa: BLE001 - reported in the line

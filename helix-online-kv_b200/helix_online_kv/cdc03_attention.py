@@ -152,6 +152,39 @@ class CDC03Cache(CompressedKVCache):
                 self._coded[layer_idx] = cold
         return self._views(layer_idx)
 
+    def state_dict(self) -> dict:
+        """The CompressedKVCache state of the exact layers, the CDC-03 store and
+        the per-layer counters, as CPU tensors."""
+        import dataclasses
+        store = {k: (v.detach().cpu() if isinstance(v, torch.Tensor) else v) for k, v in self.store.state_dict().items()}
+        return {"config": dataclasses.asdict(self.config), "n_layers": self.n_layers_expected,
+                "total_tokens": self._total_tokens, "calibration_stats": list(self._calibration_stats),
+                "layer_states": [ls.state_dict() for ls in self.layer_states],
+                "exact_kv": self._exact_layers_state(skip=self._slot), "store": store,
+                "len": list(self._len), "coded": list(self._coded), "calibrated": list(self._calibrated),
+                "budget": (self.top_k, self.sink_tokens, self.hot_window)}
+
+    def load_state_dict(self, state: dict) -> None:
+        import dataclasses
+        mine = dataclasses.asdict(self.config)
+        if state["config"] != mine or state["n_layers"] != self.n_layers_expected:
+            raise ValueError(f"Expected shape {(mine, self.n_layers_expected)}, got "
+                             f"{(state['config'], state['n_layers'])}")
+        self.store.load_state_dict(state["store"])
+        self._total_tokens = int(state["total_tokens"])
+        self._calibration_stats = list(state["calibration_stats"])
+        for ls, st in zip(self.layer_states, state["layer_states"]):
+            ls.load_state_dict(st)
+        self._load_exact_kv(state["exact_kv"], skip=self._slot)
+        self._len, self._coded, self._calibrated = list(state["len"]), list(state["coded"]), list(state["calibrated"])
+        self.top_k, self.sink_tokens, self.hot_window = state["budget"]
+        for i in self._slot:
+            layer = _StoreLayer(self, i)
+            if self._len[i] > 0:
+                layer.dtype, layer.device, layer.is_initialized = self.store.k.dtype, self.store.k.device, True
+                layer.keys, layer.values = self._views(i)
+            self.layers[i] = layer
+
     def memory_report(self) -> dict:
         """Device bytes: exact layers in the parent, the store's exact tiers for
         compressed layers, and their PQ codes and codebooks; the keys of the

@@ -67,6 +67,28 @@ class OnlineCodebook:
         self._cent_dev = dev
         self._centroids = dev.cpu().numpy()
 
+    # ---- checkpoint / resume (the reference has no serialization) ------------
+    _PARAMS = ("n_clusters", "max_iters", "rtol", "drift_threshold", "drift_ema_alpha")
+
+    def state_dict(self) -> dict:
+        """Parameters, phase, centroids and pending calibration values, as CPU tensors."""
+        buf = [p.reshape(-1).float().cpu() if _is_tensor(p) else torch.from_numpy(np.asarray(p, np.float32).ravel())
+               for p in self._calibration_buffer]
+        return {"params": {k: getattr(self, k) for k in self._PARAMS}, "finalized": self._finalized,
+                "centroids": None if self._cent_dev is None else self._cent_dev.detach().cpu(),
+                "calibration": torch.cat(buf) if buf else None}
+
+    def load_state_dict(self, state: dict) -> None:
+        mine = {k: getattr(self, k) for k in self._PARAMS}
+        if state["params"] != mine:
+            raise ValueError(f"Expected parameters {mine}, got {state['params']}")
+        self._calibration_buffer = [] if state["calibration"] is None else [state["calibration"].clone()]
+        self._finalized = bool(state["finalized"])
+        if state["centroids"] is None:
+            self._cent_dev, self._centroids = None, None
+        else:
+            self._set_centroids_dev(L.to_dev(state["centroids"]))
+
     def feed_calibration(self, values) -> None:
         """Accumulate calibration values (codebook.py:47-55)."""
         if self._finalized:

@@ -76,6 +76,51 @@ class CompressedKVCache(DynamicCache):
         self._calibration_stats.extend(ls.feed_tokens(k_rows, v_rows))
         return k_out, v_out
 
+    # ---- checkpoint / resume (the reference has no serialization) ------------
+    def _exact_layers_state(self, skip=()):
+        out = []
+        for i, layer in enumerate(getattr(self, "layers", [])):
+            k, v = getattr(layer, "keys", None), getattr(layer, "values", None)
+            if i in skip or not isinstance(k, torch.Tensor) or k.numel() == 0:
+                out.append(None)
+            else:
+                out.append((k.detach().cpu(), v.detach().cpu()))
+        return out
+
+    def state_dict(self) -> dict:
+        """Configuration, token count, every layer state (codebooks and indices)
+        and the exact K/V the parent DynamicCache holds, as CPU tensors."""
+        import dataclasses
+        return {"config": dataclasses.asdict(self.config), "n_layers": self.n_layers_expected,
+                "total_tokens": self._total_tokens, "calibration_stats": list(self._calibration_stats),
+                "layer_states": [ls.state_dict() for ls in self.layer_states],
+                "exact_kv": self._exact_layers_state()}
+
+    def _load_exact_kv(self, exact_kv, skip=()):
+        from transformers.cache_utils import DynamicLayer
+        from . import _lib as L
+        for i, kv in enumerate(exact_kv):
+            if i in skip:
+                continue
+            while len(self.layers) <= i:
+                self.layers.append(DynamicLayer())
+            layer = DynamicLayer()
+            if kv is not None:
+                layer.update(L.to_dev(kv[0], kv[0].dtype), L.to_dev(kv[1], kv[1].dtype))
+            self.layers[i] = layer
+
+    def load_state_dict(self, state: dict) -> None:
+        import dataclasses
+        mine = dataclasses.asdict(self.config)
+        if state["config"] != mine or state["n_layers"] != self.n_layers_expected:
+            raise ValueError(f"Expected shape {(mine, self.n_layers_expected)}, got "
+                             f"{(state['config'], state['n_layers'])}")
+        self._total_tokens = int(state["total_tokens"])
+        self._calibration_stats = list(state["calibration_stats"])
+        for ls, st in zip(self.layer_states, state["layer_states"]):
+            ls.load_state_dict(st)
+        self._load_exact_kv(state["exact_kv"])
+
     def memory_report(self) -> dict:
         """Exact (parent) and compressed bytes (compressed_cache.py:107-130)."""
         compressed = sum(ls.memory_bytes()["total_bytes"] for ls in self.layer_states)

@@ -155,6 +155,43 @@ class KVLayerState:
             return None
         return self.v_codebook.decode(self._stack(self._v_indices))
 
+    # ---- checkpoint / resume (the reference has no serialization) ------------
+    def state_dict(self) -> dict:
+        """Phase, counters, both codebooks and the index blocks (CPU uint8)."""
+        def blocks(parts):
+            if not parts:
+                return None
+            if isinstance(parts[0], np.ndarray):
+                return ("numpy", torch.from_numpy(np.stack(parts)))
+            return ("device", torch.cat([p.reshape(-1, p.shape[-1]) for p in parts], 0).cpu())
+        return {"layer_idx": self.layer_idx, "phase": self.phase.value, "tokens_seen": self._tokens_seen,
+                "n_compressed": self._n_compressed,
+                "k_codebook": None if self.k_codebook is None else self.k_codebook.state_dict(),
+                "v_codebook": None if self.v_codebook is None else self.v_codebook.state_dict(),
+                "k_indices": blocks(self._k_indices), "v_indices": blocks(self._v_indices)}
+
+    def load_state_dict(self, state: dict) -> None:
+        if state["layer_idx"] != self.layer_idx or (state["phase"] == LayerPhase.EXACT.value) != self.is_exact:
+            raise ValueError(f"Expected shape of layer {self.layer_idx} ({self.phase.value}), got layer "
+                             f"{state['layer_idx']} ({state['phase']})")
+        self.phase = LayerPhase(state["phase"])
+        self._tokens_seen = int(state["tokens_seen"])
+        self._n_compressed = int(state["n_compressed"])
+        for name in ("k_codebook", "v_codebook"):
+            if state[name] is not None:
+                getattr(self, name).load_state_dict(state[name])
+
+        def unblock(b):
+            if b is None:
+                return []
+            kind, t = b
+            if kind == "numpy":
+                return [row for row in t.numpy()]
+            from . import _lib as L
+            return [L.to_dev(t, torch.uint8)]
+        self._k_indices = unblock(state["k_indices"])
+        self._v_indices = unblock(state["v_indices"])
+
     def memory_bytes(self) -> dict:
         """Codebook and index bytes of this layer (layer_state.py:164-182)."""
         if self.phase == LayerPhase.EXACT:

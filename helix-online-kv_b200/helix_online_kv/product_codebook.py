@@ -170,6 +170,37 @@ class ProductCodebook:
         if not self._finalized:
             raise RuntimeError(msg)
 
+    # ---- checkpoint / resume (the reference has no serialization) ------------
+    _PARAMS = ("n_subspaces", "sub_clusters", "head_dim", "max_iters", "rtol")
+
+    def state_dict(self) -> dict:
+        """Parameters, phase, the M sub-codebooks (slots and counts) and pending
+        calibration vectors, as CPU tensors."""
+        buf = [p.float().cpu() if _is_tensor(p) else torch.from_numpy(np.asarray(p, np.float32)) for p in self._buffer]
+        return {"params": {k: getattr(self, k) for k in self._PARAMS}, "finalized": self._finalized,
+                "centroids": None if self._cents_dev is None else self._cents_dev.detach().cpu(),
+                "counts": None if self._k_dev is None else self._k_dev.detach().cpu(),
+                "calibration": torch.cat(buf, 0) if buf else None}
+
+    def load_state_dict(self, state: dict) -> None:
+        mine = {k: getattr(self, k) for k in self._PARAMS}
+        if state["params"] != mine:
+            raise ValueError(f"Expected parameters {mine}, got {state['params']}")
+        self._buffer = [] if state["calibration"] is None else [state["calibration"].clone()]
+        for cb in self._codebooks:
+            cb._calibration_buffer = [None] * len(self._buffer)
+        self._finalized = bool(state["finalized"])
+        if state["centroids"] is None:
+            self._cents_dev = self._k_dev = self._k_host = None
+            return
+        self._cents_dev = L.to_dev(state["centroids"])
+        self._k_dev = L.to_dev(state["counts"], torch.int32)
+        self._k_host = state["counts"].numpy().astype(np.int32)
+        host_c = state["centroids"].numpy()
+        for s, cb in enumerate(self._codebooks):
+            cb._calibration_buffer = []
+            cb._adopt(self._cents_dev[s:s + 1], self._k_dev[s:s + 1], host_c[s, :self._k_host[s]].copy(), None)
+
     def assign(self, vectors):
         """[N, M] uint8 codes (product_codebook.py:118-145)."""
         self._require("ProductCodebook not finalized -- call finalize_calibration() first")

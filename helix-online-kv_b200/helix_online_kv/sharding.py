@@ -1,12 +1,15 @@
-"""Sequence sharding across GPUs (one process per GPU).
+"""Sequence and KV-head sharding across GPUs (one process per GPU).
 
 Every (sequence, layer, KV head) unit of the compressed KV path is independent
-(compressed_attention.py:21-22 keeps no cross-head state), so a batch is split
-by sequence: rank r owns a contiguous block of sequences, holds their tiers in
-its own HBM and decodes them with no data-path collective.  The only
-collectives are for reporting: the max over ranks of a device time and an
-all-gather of per-step outputs.  They run over NCCL between GPUs and over gloo
-on CPU (tests).
+(compressed_attention.py:21-22 keeps no cross-head state).  A batch is split
+by sequence (the primary partition): rank r owns a contiguous block of
+sequences, holds their tiers in its own HBM and decodes them with no
+data-path collective; per-step outputs are all-gathered for reporting.  With
+fewer sequences than GPUs the KV heads are split instead (the secondary
+partition): rank r owns a contiguous block of KV heads and their query heads,
+and every layer's attention outputs [B, H_q, D] are all-gathered along the
+head axis.  The collectives run over NCCL between GPUs and over gloo on CPU
+(tests).
 """
 
 from __future__ import annotations
@@ -56,3 +59,25 @@ def gather_outputs(local: torch.Tensor) -> torch.Tensor:
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad)
     return torch.cat([p[:s] for p, s in zip(parts, sizes)], dim=0)
+
+
+def head_shard(n_kv_heads: int, world: int, rank: int) -> range:
+    """KV heads [start, stop) owned by `rank` in the head partition (the same
+    contiguous split as shard_range)."""
+    return shard_range(n_kv_heads, world, rank)
+
+
+def gather_heads(local: torch.Tensor, n_kv_heads: int, q_per_kv: int) -> torch.Tensor:
+    """Reassemble [B, H_q, D] attention outputs from every rank's [B, G * h_r, D]
+    block (h_r = the rank's KV heads, G = q_per_kv query heads per KV head), in
+    head order.  A rank may own no head (fewer KV heads than ranks)."""
+    if not _ready():
+        return local
+    world = dist.get_world_size()
+    counts = [len(head_shard(n_kv_heads, world, r)) * q_per_kv for r in range(world)]
+    mx = max(counts)
+    pad = torch.zeros((local.shape[0], mx) + tuple(local.shape[2:]), dtype=local.dtype, device=local.device)
+    pad[:, :local.shape[1]] = local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad.contiguous())
+    return torch.cat([p[:, :c] for p, c in zip(parts, counts)], dim=1)

@@ -48,6 +48,33 @@ class VectorCodebook:
         self._finalized = True
         return stats
 
+    # ---- checkpoint / resume (the reference has no serialization) ------------
+    _PARAMS = ("n_clusters", "head_dim", "max_iters", "rtol")
+
+    def state_dict(self) -> dict:
+        """Parameters, phase, centroid slots and counts, pending calibration vectors (CPU tensors)."""
+        buf = [p.float().cpu() if _is_tensor(p) else torch.from_numpy(np.asarray(p, np.float32))
+               for p in self._calibration_buffer if p is not None]
+        return {"params": {k: getattr(self, k) for k in self._PARAMS}, "finalized": self._finalized,
+                "centroids": None if self._cents_dev is None else self._cents_dev.detach().cpu(),
+                "counts": None if self._k_dev is None else self._k_dev.detach().cpu(),
+                "calibration": torch.cat(buf, 0) if buf else None}
+
+    def load_state_dict(self, state: dict) -> None:
+        mine = {k: getattr(self, k) for k in self._PARAMS}
+        if state["params"] != mine:
+            raise ValueError(f"Expected parameters {mine}, got {state['params']}")
+        self._calibration_buffer = [] if state["calibration"] is None else [state["calibration"].clone()]
+        self._finalized = bool(state["finalized"])
+        if state["centroids"] is None:
+            self._cents_dev = self._k_dev = self._centroids = None
+        else:
+            self._cents_dev = L.to_dev(state["centroids"])
+            self._k_dev = L.to_dev(state["counts"], torch.int32)
+            kk = int(state["counts"].reshape(-1)[0])
+            self._centroids = state["centroids"].reshape(-1, state["centroids"].shape[-2],
+                                                         self.head_dim)[0, :kk].numpy().copy()
+
     def _check_shape(self, v):
         if v.ndim != 2 or v.shape[1] != self.head_dim:
             raise ValueError(f"Expected shape [N, {self.head_dim}], got {tuple(v.shape)}")
