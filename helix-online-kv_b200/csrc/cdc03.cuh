@@ -197,6 +197,32 @@ __device__ __forceinline__ QuantScale quant_scale(const float* lo, const float* 
   return r;
 }
 
+// quant_scale computed by one warp: lane s takes subspace s (and s + 32), the
+// largest range and the sum of max(|lo|, |hi|) are warp reductions.  Every
+// lane returns the result.
+__device__ __forceinline__ QuantScale quant_scale_warp(const float* lo, const float* hi, int M, float scale,
+                                                       int lane) {
+  const int qmax = qmax_for(M);
+  float rmax = 0.f;
+  double sa = 0.0;
+  for (int s = lane; s < M; s += 32) {
+    rmax = fmaxf(rmax, hi[s] - lo[s]);
+    sa += fmax(fabs((double)lo[s]), fabs((double)hi[s]));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+  }
+  const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
+  const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
+  const bool ok_scale = (scale > 0.f) && isfinite(scale) && isfinite(sa);
+  QuantScale r;
+  r.inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
+  r.margin = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
+  return r;
+}
+
 __device__ __forceinline__ uint16_t quant_code(float t, float lo, float inv, int qmax) {
   float x = __fmul_rn(__fsub_rn(t, lo), inv);
   x = fminf(fmaxf(rintf(x), 0.f), (float)qmax);
@@ -367,28 +393,29 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
 // ===========================================================================
 constexpr int K5_THREADS = 512;
 
+constexpr int K5_FIRST_ROWS = 128;   // codebook rows read before the live counts are known
+
 template <int CS, int GT, int SD>
 __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, float* sq) {
   constexpr int TPS = K5_THREADS / CS;   // threads per column
   constexpr int NS = 256 / TPS;          // row slots per thread
   __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
   __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int s = tid % CS, r0 = tid / CS;
   const int M = p.M;
   const float* col = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh + (int64_t)(s < M ? s : 0) * p.slots * SD;
+  // every independent load first: live count, the first rows, the queries, the length
   int ks = 0;
-  if (s < M) {
-    ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
-    ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-  }
+  if (s < M) ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
+  const int first = min(p.slots, K5_FIRST_ROWS);
   // rows in registers NB at a time (all of them for sub_dim <= 8)
   constexpr int NB = (SD <= 8) ? NS : ((64 / SD) < 1 ? 1 : (64 / SD) > NS ? NS : (64 / SD));
-  auto load_rows = [&](int i0, float (&c)[NB][SD]) {
+  auto load_rows = [&](int i0, float (&c)[NB][SD], int lo_row, int hi_row) {
 #pragma unroll
     for (int i = 0; i < NB; ++i) {
       const int j = r0 + (i0 + i) * TPS;
-      if (i0 + i < NS && j < ks) {
+      if (i0 + i < NS && j >= lo_row && j < hi_row) {
 #pragma unroll
         for (int d = 0; d < SD; d += 4) {
           const float4 v = __ldg(reinterpret_cast<const float4*>(col + (int64_t)j * SD + d));
@@ -398,11 +425,15 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     }
   };
   float c[NB][SD];
-  load_rows(0, c);
+  if (s < M) load_rows(0, c, 0, first);
   for (int i = tid; i < GT * p.D; i += K5_THREADS) {
     const int g = i / p.D, d = i - g * p.D;
     sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
   }
+  const ColdRange cr = cold_range(p, b);
+  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking: k6 and k7 read no table (the same in every thread)
+  ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
+  if (s < M && ks > first) load_rows(0, c, first, ks);   // live rows past the first ones (large codebooks)
   if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
   __syncthreads();
   stamp(2, blockIdx.x, 1);   // queries staged
@@ -413,7 +444,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
   const int64_t tx = (int64_t)u * GT * CS * 256;
 #pragma unroll
   for (int i0 = 0; i0 < NS; i0 += NB) {
-    if (i0 > 0) load_rows(i0, c);
+    if (i0 > 0 && s < M) load_rows(i0, c, 0, ks);
 #pragma unroll
     for (int g = 0; g < GT; ++g) {
       float qs[SD];
@@ -462,10 +493,12 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     }
   }
   __syncthreads();
-  if (tid < GT) {
-    const QuantScale qsc = quant_scale(f_lo[tid], f_hi[tid], M, p.scale);
-    s_inv[tid] = qsc.inv;
-    p.margin[(int64_t)u * GT + tid] = qsc.margin;
+  if (warp < GT) {   // one warp per head
+    const QuantScale qsc = quant_scale_warp(f_lo[warp], f_hi[warp], M, p.scale, lane);
+    if (lane == 0) {
+      s_inv[warp] = qsc.inv;
+      p.margin[(int64_t)u * GT + warp] = qsc.margin;
+    }
   }
   __syncthreads();
   unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
@@ -478,17 +511,16 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     put_entry<CS, GT>(gimg, s, r0 + i * TPS, code);
   }
   stamp(2, blockIdx.x, 3);   // image stored
+  __syncthreads();
+  pdl_launch_dependents();   // k6 may launch now: it waits for this grid's memory before reading the image
 }
 
 template <int CS, int GT>
 __global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
   extern __shared__ __align__(16) float k5_sq[];   // [GT][D] queries
-  pdl_launch_dependents();   // k6 may start: it prefetches its codes, then waits for this grid
   stamp(2, blockIdx.x, 0);
   const int u = blockIdx.x;
   const int b = u / p.Hkv, h = u - b * p.Hkv;
-  const ColdRange cr = cold_range(p, b);
-  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking: k6 and k7 read no table
   switch (p.sd) {
     case 4: k5_body<CS, GT, 4>(p, u, b, h, k5_sq); break;
     case 8: k5_body<CS, GT, 8>(p, u, b, h, k5_sq); break;
