@@ -44,9 +44,8 @@
 
 namespace hokv {
 
-constexpr int TC_ROWS = 128;          // rows per tile = TMEM lanes = threads
-constexpr int TC_THREADS = 128;
-constexpr int TC_TMEM_COLS = 256;     // fp32 accumulator columns (centroid slots)
+constexpr int TC_ROWS = 128;          // rows per tile = TMEM lanes = epilogue threads
+constexpr int TC_TMEM_COLS = 256;     // fp32 accumulator columns: two stages of 128 or one of 256
 constexpr int TC_MIN_ROWS = 256;      // smaller batches stay on the CUDA-core kernels
 constexpr unsigned long long TC_WAIT_NS = 1000000000ull;   // an mbarrier wait gives up after one second
 
@@ -147,49 +146,104 @@ __device__ __forceinline__ uint32_t cm_off(int r, int k, int ke) {
   return (uint32_t)((r >> 3) * (ke >> 2) * 128 + (k >> 2) * 128 + (r & 7) * 16 + (k & 3) * 4);
 }
 
-// grid (M, tile groups, n_sets), TC_THREADS threads.  KX = ceil(SD / 8) K
-// slices of x; shared memory: A [128][KA] (x_hi, [1, 1, 0..], x_lo), B_hi
-// [256][KE] (c_hi, norms), B_lo [256][KL] (c_lo), with KL = 8 KX,
-// KE = KL + 8, KA = 2 KL + 8; |c|^2 [256], then the control words.
-template <int SD>
-__global__ void __launch_bounds__(TC_THREADS) k_pq_assign_tc(const void* __restrict__ x, int dtype, int64_t n,
-                                                           int64_t xrs, int64_t xss, const float* __restrict__ cents,
-                                                           int slots, int64_t css, const int* __restrict__ kk,
-                                                           int64_t kss, uint8_t* __restrict__ out, int64_t ors,
-                                                           int64_t oss) {
-  constexpr int KX = (SD + 7) / 8;
-  constexpr int KL = 8 * KX;
-  constexpr int KE = KL + 8;
-  constexpr int KA = 2 * KL + 8;
-  extern __shared__ __align__(1024) unsigned char tc_smem[];
-  unsigned char* sA = tc_smem;                              // 128 x KA
-  unsigned char* sBh = sA + TC_ROWS * KA * 4;               // 256 x KE
-  unsigned char* sBl = sBh + 256 * KE * 4;                  // 256 x KL
-  float* csq = reinterpret_cast<float*>(sBl + 256 * KL * 4);   // [256]
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(csq + 256);
-  uint32_t* ctl = reinterpret_cast<uint32_t*>(mbar + 1);   // [0] tmem base, [1] Cmax ord, [2] Csq_max ord, [3] failed
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(mbar)) : "memory");
+}
 
-  const int s = blockIdx.x, set = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5;
+constexpr int TC_PRODUCERS = 64;      // threads (two warps) filling A tiles
+constexpr int TC_CTA = TC_ROWS + TC_PRODUCERS + 32;   // 4 epilogue warps, 2 producer warps, 1 MMA warp
+
+// Tile geometry of k_pq_assign_tc: K slices of x (KX), B and A row lengths,
+// and the A ring depth that keeps two CTAs per SM where it can (at most 113 KB
+// of shared memory each), one otherwise; STAGES == 0 marks a variant that does
+// not fit (the CUDA-core kernel handles it).
+template <int SD, bool SPLIT>
+struct TcGeo {
+  static constexpr int KX = (SD + 7) / 8;
+  static constexpr int KL = 8 * KX;
+  static constexpr int KE = KL + 8;
+  static constexpr int KA = SPLIT ? 2 * KL + 8 : KL + 8;
+  static constexpr int A_BYTES = TC_ROWS * KA * 4;
+  static constexpr int SIDE_BYTES = TC_ROWS * (SD + 2) * 4;
+  static constexpr int FIXED = 256 * KE * 4 + 256 * KL * 4 + 256 * 4 + 256;
+  static constexpr int PER = A_BYTES + SIDE_BYTES;
+  static constexpr int S2 = (113 * 1024 - FIXED) / PER;
+  static constexpr int S1 = (227 * 1024 - FIXED) / PER;
+  static constexpr int STAGES = S2 >= 2 ? (S2 > 4 ? 4 : S2) : (S1 >= 1 ? (S1 > 4 ? 4 : S1) : 0);
+  static constexpr int SMEM = FIXED + (STAGES > 0 ? STAGES : 1) * PER;
+};
+
+// grid (CTAs), TC_CTA threads; CTA c takes (set, subspace) pair c % pairs and
+// tile group c / pairs.  Roles:
+//   warps 0-3  epilogue: thread r owns row r of a tile (TMEM lane r);
+//   warps 4-5  producers: x rows of the next tiles into a TC_STAGES ring of
+//              A tiles (x_hi, [1, 1, 0..], x_lo in core-matrix layout) plus
+//              the fp32 row, |x|^2 and |x|_1 the epilogue needs;
+//   warp 6     lane 0 issues the MMAs of a tile into one of the accumulator
+//              stages (two of 128 columns, or one of 256 when more than 128
+//              centroids are live) and commits them to that stage's mbarrier.
+// mbarriers: a_full[s] (64 producer arrivals), a_empty[s] (4 epilogue warps),
+// acc_full[a] (the commit), acc_empty[a] (4 epilogue warps).  Every wait is
+// bounded; a wait that gives up sets HOKV_ERR_TIMEOUT and the CTA drains.
+// Shared memory: B_hi [256][KE], B_lo [256][KL], |c|^2 [256], then per stage
+// A [128][KA] and the rows [128][SD] + |x|^2 [128] + |x|_1 [128], then the
+// barriers and control words.
+template <int SD, bool SPLIT>
+__global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restrict__ x, int dtype, int64_t n, int64_t xrs,
+                                                          int64_t xss, const float* __restrict__ cents, int slots,
+                                                          int64_t css, const int* __restrict__ kk, int64_t kss,
+                                                          uint8_t* __restrict__ out, int64_t ors, int64_t oss, int M,
+                                                          int n_sets, int groups) {
+  using TG = TcGeo<SD, SPLIT>;
+  constexpr int KX = TG::KX, KL = TG::KL, KE = TG::KE, KA = TG::KA;
+  constexpr int A_BYTES = TG::A_BYTES, SIDE_BYTES = TG::SIDE_BYTES, TC_STAGES = TG::STAGES;
+  static_assert(TC_STAGES >= 1, "variant does not fit in shared memory");
+  extern __shared__ __align__(1024) unsigned char tc_smem[];
+  unsigned char* sBh = tc_smem;                                  // 256 x KE
+  unsigned char* sBl = sBh + 256 * KE * 4;                       // 256 x KL
+  float* csq = reinterpret_cast<float*>(sBl + 256 * KL * 4);     // [256]
+  unsigned char* ring = reinterpret_cast<unsigned char*>(csq + 256);   // TC_STAGES x (A, side)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + TC_STAGES * (A_BYTES + SIDE_BYTES));
+  uint64_t* a_full = bars;
+  uint64_t* a_empty = bars + TC_STAGES;
+  uint64_t* acc_full = bars + 2 * TC_STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* ctl = reinterpret_cast<uint32_t*>(acc_empty + 2);   // [0] tmem, [1] Cmax, [2] Csq_max, [3] abort
+
+  const int pairs = M * n_sets;
+  const int pair = blockIdx.x % pairs, grp = blockIdx.x / pairs;
+  const int s = pair % M, set = pair / M;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int k = kk[(int64_t)set * kss + s];
   k = k < 1 ? 1 : (k > slots ? slots : k);
-  const int np = (k + 15) & ~15;                            // MMA N: live slots rounded up to 16
+  const int np = (k + 15) & ~15;                  // MMA N
+  const int n_acc = np <= 128 ? 2 : 1;            // accumulator stages in the 256 columns
   const float* cg = cents + (int64_t)set * css + (int64_t)s * slots * SD;
+  const int64_t n_tiles = (n + TC_ROWS - 1) / TC_ROWS;
+  const int64_t t_begin = n_tiles * grp / groups, t_end = n_tiles * (grp + 1) / groups;
+  constexpr bool split = SPLIT;                   // fp32 inputs: x = x_hi + x_lo
 
-  if (warp == 0) {   // tensor memory for the accumulator (the whole warp allocates)
+  if (warp == 6) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(ctl)),
                  "r"(TC_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(mbar, 1);
+    for (int i = 0; i < TC_STAGES; ++i) {
+      mbar_init(&a_full[i], TC_PRODUCERS);
+      mbar_init(&a_empty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
     ctl[1] = 0u;
     ctl[2] = 0u;
     ctl[3] = 0u;
   }
   __syncthreads();
-  // B: split centroids, norms, bounds
-  for (int j = tid; j < 256; j += TC_THREADS) {
+  // B: split centroids, exact norms, bounds (slots past the live count never win)
+  for (int j = tid; j < 256; j += TC_CTA) {
     float c[SD];
     const bool live = j < k;
 #pragma unroll
@@ -218,121 +272,167 @@ __global__ void __launch_bounds__(TC_THREADS) k_pq_assign_tc(const void* __restr
       atomicMax(&ctl[2], __float_as_uint(c2));
     }
   }
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl[0];
   const float cmax = __uint_as_float(ctl[1]), csqmax = __uint_as_float(ctl[2]);
-  const uint32_t idesc = umma_idesc_tf32(np);
-  const uint32_t aA = smem_u32(sA), aBh = smem_u32(sBh), aBl = smem_u32(sBl);
-  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-  constexpr float N_TERMS = 3 * KL + 2;
-  const bool split = dtype == HOKV_F32;   // fp32 inputs: x = x_hi + x_lo
+  volatile uint32_t* abort_flag = &ctl[3];
+  auto give_up = [&]() { if (atomicExch(const_cast<uint32_t*>(abort_flag), 1u) == 0u) dev_flag(HOKV_ERR_TIMEOUT); };
 
-  const int64_t n_tiles = (n + TC_ROWS - 1) / TC_ROWS;
-  unsigned phase = 0;
-  for (int64_t tile = blockIdx.y; tile < n_tiles; tile += gridDim.y) {
-    const int64_t i = tile * TC_ROWS + tid;
-    const bool valid = i < n;
-    // A row of this thread: x slice, then [1, 1, 0..]
-    float xv[SD];
-    const int64_t base = (int64_t)set * xss + (valid ? i : 0) * xrs + (int64_t)s * SD;
-#pragma unroll
-    for (int d = 0; d < SD; ++d) xv[d] = valid ? load_as_f32(x, dtype, base + d) : 0.f;
-    float xa = 0.f;
-#pragma unroll
-    for (int d = 0; d < KL; ++d) {
-      const float v = d < SD ? xv[d] : 0.f;
-      const float hi = split ? tf32_round(v) : v;
-      *reinterpret_cast<float*>(sA + cm_off(tid, d, KA)) = hi;
-      *reinterpret_cast<float*>(sA + cm_off(tid, KL + 8 + d, KA)) = v - hi;
-      xa += fabsf(v);
-    }
-#pragma unroll
-    for (int d = 0; d < 8; ++d) *reinterpret_cast<float*>(sA + cm_off(tid, KL + d, KA)) = d < 2 ? 1.f : 0.f;
-    const float x2 = sum_sq(xv, SD);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
+  if (warp < 4) {
+    // ---- epilogue: one row per thread ----------------------------------------
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    constexpr float N_TERMS = 3 * KL + 2;
+    const int nch = (np + 31) >> 5;
+    int64_t it = 0;
+    for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
+      const int st = (int)(it % TC_STAGES), a = (int)(it % n_acc);
+      const unsigned ph_a = (unsigned)((it / n_acc) & 1);
+      if (*abort_flag || !mbar_wait(&a_full[st], (unsigned)((it / TC_STAGES) & 1)) || !mbar_wait(&acc_full[a], ph_a)) {
+        give_up();
+        break;
+      }
       tc_fence_after();
-      constexpr uint32_t sbo_a = (KA / 4) * 128, sbo_h = (KE / 4) * 128, sbo_l = (KL / 4) * 128;
+      const float* side = reinterpret_cast<const float*>(ring + st * (A_BYTES + SIDE_BYTES) + A_BYTES);
+      float xv[SD];
 #pragma unroll
-      for (int kc = 0; kc < KX; ++kc)   // x_hi . c_hi
-        umma_tf32(tmem, umma_desc(aA + kc * 256, sbo_a), umma_desc(aBh + kc * 256, sbo_h), idesc, kc > 0);
-      // [1, 1, 0..] . [-|c|^2_hi / 2, -|c|^2_lo / 2, 0..]
-      umma_tf32(tmem, umma_desc(aA + KX * 256, sbo_a), umma_desc(aBh + KX * 256, sbo_h), idesc, 1);
+      for (int d = 0; d < SD; ++d) xv[d] = side[tid * SD + d];
+      const float x2 = side[TC_ROWS * SD + tid], xa = side[TC_ROWS * (SD + 1) + tid];
+      const uint32_t col0 = lane_base + (uint32_t)(a * 128);
+      float cmaxs[8];
+      float m = -INFINITY;
 #pragma unroll
-      for (int kc = 0; kc < KX; ++kc)   // x_hi . c_lo
-        umma_tf32(tmem, umma_desc(aA + kc * 256, sbo_a), umma_desc(aBl + kc * 256, sbo_l), idesc, 1);
-      if (split) {
+      for (int c = 0; c < 8; ++c) {
+        cmaxs[c] = -INFINITY;
+        if (c < nch) {
+          float v[32];
+          tmem_ld32(col0 + c * 32, v);
+          float mc = -INFINITY;
 #pragma unroll
-        for (int kc = 0; kc < KX; ++kc)   // x_lo . c_hi
-          umma_tf32(tmem, umma_desc(aA + (KX + 1 + kc) * 256, sbo_a), umma_desc(aBh + kc * 256, sbo_h), idesc, 1);
+          for (int q = 0; q < 32; ++q) mc = fmaxf(mc, (c * 32 + q < np) ? v[q] : -INFINITY);
+          cmaxs[c] = mc;
+          m = fmaxf(m, mc);
+        }
       }
-      umma_commit(mbar);
-    }
-    const bool ok = mbar_wait(mbar, phase);
-    if (__syncthreads_or(!ok)) {   // the same answer in every thread
-      if (tid == 0) { dev_flag(HOKV_ERR_TIMEOUT); ctl[3] = 1u; }
-      (void)mbar_wait(mbar, phase);   // the MMAs may still be running: one more bounded wait
-      break;
-    }
-    phase ^= 1u;
-    tc_fence_after();
-    // pass 1: the row's largest screen value and each 32-column chunk's
-    const int nch = (np + 31) >> 5;   // 32-column chunks holding the np MMA columns
-    float cmaxs[8];
-    float m = -INFINITY;
+      const float e_tc = (N_TERMS + 2.f) * 0x1p-22f * (3.f * xa * cmax + csqmax);
+      const float e_ex = 0x1p-22f * ((float)(SD + 1) * xa * cmax + x2 + csqmax);
+      const float thr = m - 1.25f * (e_ex + 2.f * e_tc);
+      float best = INFINITY;
+      int bj = 0x7fffffff;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      cmaxs[c] = -INFINITY;
-      if (c < nch) {
-        float v[32];
-        tmem_ld32(lane_base + c * 32, v);
-        float mc = -INFINITY;
+      for (int c = 0; c < 8; ++c) {
+        const bool need = c < nch && cmaxs[c] >= thr;
+        if (__any_sync(0xffffffffu, need)) {
+          float v[32];
+          tmem_ld32(col0 + c * 32, v);
+          if (need) {
+            for (int q = 0; q < 32; ++q) {
+              const int j = c * 32 + q;
+              if (j < k && v[q] >= thr) {
+                float acc = 0.f;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) mc = fmaxf(mc, (c * 32 + q < np) ? v[q] : -INFINITY);
-        cmaxs[c] = mc;
-        m = fmaxf(m, mc);
-      }
-    }
-    const float e_tc = (N_TERMS + 2.f) * 0x1p-22f * (3.f * xa * cmax + csqmax);
-    const float e_ex = 0x1p-22f * ((float)(SD + 1) * xa * cmax + x2 + csqmax);
-    const float thr = m - 1.25f * (e_ex + 2.f * e_tc);
-    // pass 2: exact distances of the candidates, ascending slot order, first minimum
-    float best = INFINITY;
-    int bj = 0x7fffffff;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const bool need = c < nch && cmaxs[c] >= thr;
-      if (__any_sync(0xffffffffu, need)) {
-        float v[32];
-        tmem_ld32(lane_base + c * 32, v);
-        if (need) {
-          for (int q = 0; q < 32; ++q) {
-            const int j = c * 32 + q;
-            if (j < k && v[q] >= thr) {
-              float acc = 0.f;
-#pragma unroll
-              for (int d = 0; d < SD; ++d) {
-                const float cd = *reinterpret_cast<const float*>(sBh + cm_off(j, d, KE)) +
-                                 *reinterpret_cast<const float*>(sBl + cm_off(j, d, KL));   // exact: c_hi + c_lo = c
-                acc = ffma(xv[d], cd, acc);
+                for (int d = 0; d < SD; ++d) {
+                  const float cd = *reinterpret_cast<const float*>(sBh + cm_off(j, d, KE)) +
+                                   *reinterpret_cast<const float*>(sBl + cm_off(j, d, KL));   // c_hi + c_lo = c
+                  acc = ffma(xv[d], cd, acc);
+                }
+                const float dd = l2_expansion(x2, acc, csq[j]);
+                if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
               }
-              const float dd = l2_expansion(x2, acc, csq[j]);
-              if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
             }
           }
         }
       }
+      const int64_t i = tile * TC_ROWS + tid;
+      if (i < n) out[(int64_t)set * oss + i * ors + s] = (uint8_t)(bj == 0x7fffffff ? 0 : bj);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[a]);
+        mbar_arrive(&a_empty[st]);
+      }
     }
-    if (valid) out[(int64_t)set * oss + i * ors + s] = (uint8_t)(bj == 0x7fffffff ? 0 : bj);
-    tc_fence_before();
-    __syncthreads();   // every lane read: the accumulator may be overwritten
+  } else if (warp < 6) {
+    // ---- producers: the next tiles' rows into the A ring -------------------
+    const int pt = tid - TC_ROWS;   // 0..63: rows pt and pt + 64 of a tile
+    int64_t it = 0;
+    for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
+      const int st = (int)(it % TC_STAGES);
+      const unsigned ph = (unsigned)(((it / TC_STAGES) & 1) ^ 1);   // the first pass finds every slot free
+      if (*abort_flag || !mbar_wait(&a_empty[st], ph)) { give_up(); break; }
+      unsigned char* A = ring + st * (A_BYTES + SIDE_BYTES);
+      float* side = reinterpret_cast<float*>(A + A_BYTES);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = pt + h * 64;
+        const int64_t i = tile * TC_ROWS + r;
+        const bool valid = i < n;
+        const int64_t base = (int64_t)set * xss + (valid ? i : 0) * xrs + (int64_t)s * SD;
+        float xv[SD];
+#pragma unroll
+        for (int d = 0; d < SD; ++d) xv[d] = valid ? load_as_f32(x, dtype, base + d) : 0.f;
+        float xa = 0.f;
+#pragma unroll
+        for (int d = 0; d < KL; ++d) {
+          const float v = d < SD ? xv[d] : 0.f;
+          const float hi = split ? tf32_round(v) : v;
+          *reinterpret_cast<float*>(A + cm_off(r, d, KA)) = hi;
+          if (split) *reinterpret_cast<float*>(A + cm_off(r, KL + 8 + d, KA)) = v - hi;
+          xa += fabsf(v);
+        }
+#pragma unroll
+        for (int d = 0; d < 8; ++d) *reinterpret_cast<float*>(A + cm_off(r, KL + d, KA)) = d < 2 ? 1.f : 0.f;
+#pragma unroll
+        for (int d = 0; d < SD; ++d) side[r * SD + d] = xv[d];
+        side[TC_ROWS * SD + r] = sum_sq(xv, SD);
+        side[TC_ROWS * (SD + 1) + r] = xa;
+      }
+      fence_async_smem();
+      mbar_arrive(&a_full[st]);
+    }
+  } else if (lane == 0) {
+    // ---- MMA issue --------------------------------------------------------------
+    const uint32_t idesc = umma_idesc_tf32(np);
+    const uint32_t aBh = smem_u32(sBh), aBl = smem_u32(sBl);
+    constexpr uint32_t sbo_a = (KA / 4) * 128, sbo_h = (KE / 4) * 128, sbo_l = (KL / 4) * 128;
+    int64_t it = 0;
+    for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
+      const int st = (int)(it % TC_STAGES), a = (int)(it % n_acc);
+      const unsigned ph_full = (unsigned)((it / TC_STAGES) & 1);
+      const unsigned ph_empty = (unsigned)(((it / n_acc) & 1) ^ 1);
+      if (*abort_flag || !mbar_wait(&a_full[st], ph_full) || !mbar_wait(&acc_empty[a], ph_empty)) {
+        give_up();
+        break;
+      }
+      tc_fence_after();
+      const uint32_t aA = smem_u32(ring + st * (A_BYTES + SIDE_BYTES));
+      const uint32_t d = tmem + (uint32_t)(a * 128);
+#pragma unroll
+      for (int kc = 0; kc < KX; ++kc)   // x_hi . c_hi
+        umma_tf32(d, umma_desc(aA + kc * 256, sbo_a), umma_desc(aBh + kc * 256, sbo_h), idesc, kc > 0);
+      // [1, 1, 0..] . [-|c|^2_hi / 2, -|c|^2_lo / 2, 0..]
+      umma_tf32(d, umma_desc(aA + KX * 256, sbo_a), umma_desc(aBh + KX * 256, sbo_h), idesc, 1);
+#pragma unroll
+      for (int kc = 0; kc < KX; ++kc)   // x_hi . c_lo
+        umma_tf32(d, umma_desc(aA + kc * 256, sbo_a), umma_desc(aBl + kc * 256, sbo_l), idesc, 1);
+      if (split) {
+#pragma unroll
+        for (int kc = 0; kc < KX; ++kc)   // x_lo . c_hi
+          umma_tf32(d, umma_desc(aA + (KX + 1 + kc) * 256, sbo_a), umma_desc(aBh + kc * 256, sbo_h), idesc, 1);
+      }
+      umma_commit(&acc_full[a]);
+    }
+    // the last commits: wait (bounded) until this thread's MMAs are done
+    if (it > 0) {
+      const int64_t last = it - 1;
+      (void)mbar_wait(&acc_full[last % n_acc], (unsigned)((last / n_acc) & 1));
+    }
   }
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 6) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
   }

@@ -317,38 +317,47 @@ int hokv_scalar_vq_qkt(const float* q, const void* idx, int idx_dtype, int64_t s
 }  // extern "C"
 
 namespace hokv {
-template <int SD>
+// HOKV_OK when launched, -1 when no tensor-core variant fits (the caller
+// takes the CUDA-core kernels), else an error status.
+template <int SD, bool SPLIT>
 static int launch_assign_tc_sd(const void* x, int x_dtype, int64_t n, int64_t xrs, int64_t xss, int M,
                                const float* cents, int slots, int64_t css, const int* k, int64_t kss, uint8_t* out,
                                int64_t ors, int64_t oss, int n_sets, cudaStream_t st) {
-  constexpr int KX = (SD + 7) / 8, KL = 8 * KX, KE = KL + 8, KA = 2 * KL + 8;
-  size_t sm = (size_t)TC_ROWS * KA * 4 + (size_t)256 * KE * 4 + (size_t)256 * KL * 4 + 256 * 4 + 64;
-  // at most two CTAs per SM: each holds TC_TMEM_COLS of the 512 tensor-memory columns
-  sm = std::max<size_t>(sm, 80 * 1024);
-  if (int e = ensure_smem(k_pq_assign_tc<SD>, sm)) return e;
-  int dev = 0, n_sm = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t n_tiles = cdiv(n, TC_ROWS);
-  const int64_t units = (int64_t)M * n_sets;
-  // about four tiles per CTA (the staged codebook is reused), at least two CTAs per SM
-  int64_t groups = std::max<int64_t>(cdiv(n_tiles, 4), cdiv(2 * n_sm, units));
-  groups = std::min<int64_t>(std::min<int64_t>(groups, n_tiles), 65535);
-  k_pq_assign_tc<SD><<<dim3((unsigned)M, (unsigned)groups, (unsigned)n_sets), TC_THREADS, sm, st>>>(
-      x, x_dtype, n, xrs, xss, cents, slots, css, k, kss, out, ors, oss);
-  return check_launch("k_pq_assign_tc");
+  using TG = TcGeo<SD, SPLIT>;
+  if constexpr (TG::STAGES == 0) {
+    return -1;
+  } else {
+    // at most two CTAs per SM: each holds TC_TMEM_COLS of the 512 tensor-memory columns
+    const size_t sm = std::max<size_t>((size_t)TG::SMEM, 80 * 1024);
+    if (int e = ensure_smem(k_pq_assign_tc<SD, SPLIT>, sm)) return e;
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t n_tiles = cdiv(n, TC_ROWS);
+    const int64_t pairs = (int64_t)M * n_sets;
+    // persistent CTAs: every (set, subspace) pair split into tile groups,
+    // about two CTAs per SM over the whole grid
+    const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(n_tiles, cdiv(2 * n_sm, pairs)));
+    if (pairs * groups > (int64_t)INT32_MAX) return fail(HOKV_ERR_UNSUPPORTED, "pq_assign: grid too large");
+    k_pq_assign_tc<SD, SPLIT><<<(unsigned)(pairs * groups), TC_CTA, sm, st>>>(
+        x, x_dtype, n, xrs, xss, cents, slots, css, k, kss, out, ors, oss, M, n_sets, (int)groups);
+    return check_launch("k_pq_assign_tc");
+  }
 }
 
 static int launch_assign_tc(const void* x, int x_dtype, int64_t n, int64_t xrs, int64_t xss, int M, int sd,
                             const float* cents, int slots, int64_t css, const int* k, int64_t kss, uint8_t* out,
                             int64_t ors, int64_t oss, int n_sets, cudaStream_t st) {
-#define HOKV_TC(sd_)                                                                                       \
-  if (sd == sd_)                                                                                          \
-    return launch_assign_tc_sd<sd_>(x, x_dtype, n, xrs, xss, M, cents, slots, css, k, kss, out, ors, oss, \
-                                    n_sets, st);
+  const bool split = x_dtype == HOKV_F32;
+#define HOKV_TC(sd_)                                                                                              \
+  if (sd == sd_)                                                                                                 \
+    return split ? launch_assign_tc_sd<sd_, true>(x, x_dtype, n, xrs, xss, M, cents, slots, css, k, kss, out, ors, \
+                                                  oss, n_sets, st)                                              \
+                 : launch_assign_tc_sd<sd_, false>(x, x_dtype, n, xrs, xss, M, cents, slots, css, k, kss, out,    \
+                                                   ors, oss, n_sets, st);
   HOKV_TC(4) HOKV_TC(8) HOKV_TC(16) HOKV_TC(32) HOKV_TC(64)
 #undef HOKV_TC
-  return fail(HOKV_ERR_UNSUPPORTED, "pq_assign: tensor-core path for sub_dim %d", sd);
+  return -1;
 }
 }  // namespace hokv
 
@@ -369,8 +378,10 @@ int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, 
       (sub_dim == 4 || sub_dim == 8 || sub_dim == 16 || sub_dim == 32 || sub_dim == 64) && M <= 65535 &&
       n_sets <= 65535) {
     // prefill-sized batches: tensor-core screen, exact rescoring
-    return launch_assign_tc(x, x_dtype, n, x_row_stride, x_set_stride, M, sub_dim, cents, cb_slots, cent_set_stride,
-                            k, k_set_stride, out, out_row_stride, out_set_stride, n_sets, S(stream));
+    const int st = launch_assign_tc(x, x_dtype, n, x_row_stride, x_set_stride, M, sub_dim, cents, cb_slots,
+                                    cent_set_stride, k, k_set_stride, out, out_row_stride, out_set_stride, n_sets,
+                                    S(stream));
+    if (st != -1) return st;
   }
   if (dot_order == DOT_SEQ_FMA && (sub_dim == 4 || sub_dim == 8)) {
     // prefill-sized batches: register-tiled kernel, same arithmetic
