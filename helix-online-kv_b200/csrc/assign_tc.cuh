@@ -101,21 +101,24 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Wait until the mbarrier's phase `parity` completes; false when TC_WAIT_NS
-// passed first.
+// passed first.  Each try_wait may suspend the thread in hardware for up to
+// 0.1 ms (its time hint), so a blocked warp issues few instructions.
 __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, unsigned parity) {
   const uint32_t a = smem_u32(mbar);
-  const unsigned long long t0 = global_ns();
-  for (;;) {
+  const uint32_t hint_ns = 100000u;
+  unsigned long long t0 = 0;
+  for (int i = 0;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(hint_ns)
         : "memory");
     if (done) return true;
-    if (global_ns() - t0 > TC_WAIT_NS) return false;
+    if (i == 0) t0 = global_ns();
+    else if (global_ns() - t0 > TC_WAIT_NS) return false;
   }
 }
 
@@ -319,30 +322,42 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
       const float e_tc = (N_TERMS + 2.f) * 0x1p-22f * (3.f * xa * cmax + csqmax);
       const float e_ex = 0x1p-22f * ((float)(SD + 1) * xa * cmax + x2 + csqmax);
       const float thr = m - 1.25f * (e_ex + 2.f * e_tc);
-      float best = INFINITY;
-      int bj = 0x7fffffff;
+      // candidates as one bit per column of each needed chunk
+      uint32_t cmask[8];
+      int total = 0;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
+        cmask[c] = 0u;
         const bool need = c < nch && cmaxs[c] >= thr;
         if (__any_sync(0xffffffffu, need)) {
           float v[32];
           tmem_ld32(col0 + c * 32, v);
           if (need) {
-            for (int q = 0; q < 32; ++q) {
-              const int j = c * 32 + q;
-              if (j < k && v[q] >= thr) {
-                float acc = 0.f;
+            uint32_t msk = 0u;
 #pragma unroll
-                for (int d = 0; d < SD; ++d) {
-                  const float cd = *reinterpret_cast<const float*>(sBh + cm_off(j, d, KE)) +
-                                   *reinterpret_cast<const float*>(sBl + cm_off(j, d, KL));   // c_hi + c_lo = c
-                  acc = ffma(xv[d], cd, acc);
-                }
-                const float dd = l2_expansion(x2, acc, csq[j]);
-                if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
-              }
-            }
+            for (int q = 0; q < 32; ++q) msk |= (uint32_t)((c * 32 + q < k) && v[q] >= thr) << q;
+            cmask[c] = msk;
+            total += __popc(msk);
           }
+        }
+      }
+      // one candidate is the minimiser; several are rescored exactly, in slot order
+      float best = INFINITY;
+      int bj = 0x7fffffff;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        for (uint32_t msk = cmask[c]; msk; msk &= msk - 1u) {
+          const int j = c * 32 + __ffs(msk) - 1;
+          if (total == 1) { bj = j; break; }
+          float acc = 0.f;
+#pragma unroll
+          for (int d = 0; d < SD; ++d) {
+            const float cd = *reinterpret_cast<const float*>(sBh + cm_off(j, d, KE)) +
+                             *reinterpret_cast<const float*>(sBl + cm_off(j, d, KL));   // c_hi + c_lo = c
+            acc = ffma(xv[d], cd, acc);
+          }
+          const float dd = l2_expansion(x2, acc, csq[j]);
+          if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
         }
       }
       const int64_t i = tile * TC_ROWS + tid;
