@@ -219,7 +219,9 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int k = kk[(int64_t)set * kss + s];
   k = k < 1 ? 1 : (k > slots ? slots : k);
-  const int np = (k + 15) & ~15;                  // MMA N
+  // MMA N: live slots rounded up to 32, so every 32-column chunk the epilogue
+  // reads holds computed values (slots past the live count score -2^98)
+  const int np = (k + 31) & ~31;
   const int n_acc = np <= 128 ? 2 : 1;            // accumulator stages in the 256 columns
   const float* cg = cents + (int64_t)set * css + (int64_t)s * slots * SD;
   const int64_t n_tiles = (n + TC_ROWS - 1) / TC_ROWS;
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
     // ---- epilogue: one row per thread ----------------------------------------
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     constexpr float N_TERMS = 3 * KL + 2;
-    const int nch = (np + 31) >> 5;
+    const int nch = np >> 5;
     int64_t it = 0;
     for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
       const int st = (int)(it % TC_STAGES), a = (int)(it % n_acc);
@@ -312,11 +314,12 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
         if (c < nch) {
           float v[32];
           tmem_ld32(col0 + c * 32, v);
-          float mc = -INFINITY;
 #pragma unroll
-          for (int q = 0; q < 32; ++q) mc = fmaxf(mc, (c * 32 + q < np) ? v[q] : -INFINITY);
-          cmaxs[c] = mc;
-          m = fmaxf(m, mc);
+          for (int w = 16; w > 1; w >>= 1)
+#pragma unroll
+            for (int q = 0; q < w; ++q) v[q] = fmaxf(v[q], v[q + w]);
+          cmaxs[c] = fmaxf(v[0], v[1]);
+          m = fmaxf(m, cmaxs[c]);
         }
       }
       const float e_tc = (N_TERMS + 2.f) * 0x1p-22f * (3.f * xa * cmax + csqmax);
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
           if (need) {
             uint32_t msk = 0u;
 #pragma unroll
-            for (int q = 0; q < 32; ++q) msk |= (uint32_t)((c * 32 + q < k) && v[q] >= thr) << q;
+            for (int q = 0; q < 32; ++q) msk |= (uint32_t)(v[q] >= thr) << q;
             cmask[c] = msk;
             total += __popc(msk);
           }

@@ -405,10 +405,20 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
   const int s = tid % CS, r0 = tid / CS;
   const int M = p.M;
   const float* col = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh + (int64_t)(s < M ? s : 0) * p.slots * SD;
+  const int first = min(p.slots, K5_FIRST_ROWS);
+  // programmatic launch: while the previous kernel drains, only L2 prefetches of
+  // this unit's first codebook rows (a prefetch never reads stale data); every
+  // load and store of this kernel follows the wait
+  if (s < M) {
+    for (int i = 0; i < NS; ++i) {
+      const int j = r0 + i * TPS;
+      if (j < first) asm volatile("prefetch.global.L2 [%0];" ::"l"(col + (int64_t)j * SD));
+    }
+  }
+  pdl_wait();
   // every independent load first: live count, the first rows, the queries, the length
   int ks = 0;
   if (s < M) ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
-  const int first = min(p.slots, K5_FIRST_ROWS);
   // rows in registers NB at a time (all of them for sub_dim <= 8)
   constexpr int NB = (SD <= 8) ? NS : ((64 / SD) < 1 ? 1 : (64 / SD) > NS ? NS : (64 / SD));
   auto load_rows = [&](int i0, float (&c)[NB][SD], int lo_row, int hi_row) {
@@ -952,6 +962,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int64_t sel_base = ((int64_t)b * Hq + hq) * sel_cap;
 
   stamp(1, blockIdx.x, 0);
+  pdl_launch_dependents();   // the next layer's k5 may start its prefetches; it waits for this grid
   for (int d = tid; d < D; d += K7_THREADS)
     s_q[d] = load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)hq * D + d);
   if (tid == 0) s_n = 0;

@@ -97,10 +97,11 @@ static int launch_ex(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st
   return check_launch(what);
 }
 
-// Stage 1: K5 (tables, one CTA per unit, ordinary launch: it reads the
-// queries) then K6 (candidates, one thread-block cluster of
-// min(chunks, K6_CLUSTER_MAX) CTAs per unit, programmatic launch: it prefetches
-// its codes while K5 runs and waits for K5 before it reads the image).
+// Stage 1: K5 (tables, one CTA per unit, programmatic launch: it prefetches
+// its codebook rows into L2 while the previous kernel of the stream drains and
+// waits for it before any other access) then K6 (candidates, one thread-block
+// cluster of min(chunks, K6_CLUSTER_MAX) CTAs per unit, programmatic launch
+// once K5 has stored its image; it waits for K5 before it reads the image).
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
@@ -108,7 +109,7 @@ static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   const size_t sm5 = (size_t)GT * p.D * 4;   // queries
   if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
   if (int e = launch_ex(k5_tables<CS, GT>, dim3((unsigned)(p.B * p.Hkv)), dim3(K5_THREADS), sm5, st, p,
-                        "k5_tables", false))
+                        "k5_tables", true))
     return e;
   const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
   const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
