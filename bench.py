@@ -806,7 +806,8 @@ def run_ours(args):
 
 
 K6_PHASES = ["wait for k5 + image to smem", "score own chunks", "pool histograms", "threshold", "list+rescore"]
-K5_PHASES = ["queries staged (rows in flight)", "entries + ranges", "image stored"]
+K5_PHASES = ["prefetch + wait for the previous kernel", "queries staged (rows in flight)", "entries + ranges",
+             "image stored"]
 K7_PHASES = ["hot window", "wait for k6", "selection", "attend selected", "combine+store"]
 
 

@@ -59,6 +59,7 @@ struct Cdc03P {
   unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (exchanged in the cluster)
   float* texact;          // [units][GT][256][CS]    exact sub-tables (K6 rescoring, K7 rescans)
   int* margin;            // [units][GT]             error band in code units
+  int* img_rows;          // [units]                 image rows k6 copies (the largest live count)
   int n_chunks, chunk, GT, qimg_bytes;
 };
 
@@ -401,6 +402,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
   constexpr int NS = 256 / TPS;          // row slots per thread
   __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
   __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
+  __shared__ int s_ks[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int s = tid % CS, r0 = tid / CS;
   const int M = p.M;
@@ -416,6 +418,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     }
   }
   pdl_wait();
+  stamp(2, blockIdx.x, 1);   // previous kernel complete
   // every independent load first: live count, the first rows, the queries, the length
   int ks = 0;
   if (s < M) ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
@@ -445,8 +448,9 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
   ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
   if (s < M && ks > first) load_rows(0, c, first, ks);   // live rows past the first ones (large codebooks)
   if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
+  if (r0 == 0) s_ks[s] = ks;
   __syncthreads();
-  stamp(2, blockIdx.x, 1);   // queries staged
+  stamp(2, blockIdx.x, 2);   // queries staged
   float e[NS][GT];
   unsigned lo[GT], hi[GT];
 #pragma unroll
@@ -472,7 +476,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
             hi[g] = max(hi[g], o);
           }
           e[i0 + i][g] = v;
-          if (s < M) p.texact[tx + ((int64_t)g * 256 + j) * CS + s] = v;
+          if (j < ks) p.texact[tx + ((int64_t)g * 256 + j) * CS + s] = v;   // live rows only
         }
       }
     }
@@ -488,12 +492,11 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     if (lane < CS && s < M) { atomicMin(&s_lo[g][s], lo[g]); atomicMax(&s_hi[g][s], hi[g]); }
   }
   __syncthreads();
-  stamp(2, blockIdx.x, 2);   // entries and ranges
+  stamp(2, blockIdx.x, 3);   // entries and ranges
   if (tid < GT * 32) {
     const int g = tid / 32, sx = tid % 32;
     if (sx < M) {
-      int kx = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + sx];
-      kx = kx < 0 ? 0 : (kx > p.slots ? p.slots : kx);
+      const int kx = s_ks[sx];
       unsigned ol = s_lo[g][sx], oh = s_hi[g][sx];
       if (kx < 256) { ol = min(ol, ord_f32(0.f)); oh = max(oh, ord_f32(0.f)); }   // zero entries of dead rows
       float fl = unord_f32(ol), fh = unord_f32(oh);
@@ -509,6 +512,11 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
       s_inv[warp] = qsc.inv;
       p.margin[(int64_t)u * GT + warp] = qsc.margin;
     }
+  } else if (warp == GT) {   // the image rows valid codes can reach: the largest live count
+    int kx = lane < M ? s_ks[lane] : 0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) kx = max(kx, __shfl_xor_sync(0xffffffffu, kx, o));
+    if (lane == 0) p.img_rows[u] = kx;
   }
   __syncthreads();
   unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
@@ -520,7 +528,7 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
     for (int g = 0; g < GT; ++g) code[g] = (s < M) ? quant_code(e[i][g], f_lo[g][s], s_inv[g], qmax) : 0u;
     put_entry<CS, GT>(gimg, s, r0 + i * TPS, code);
   }
-  stamp(2, blockIdx.x, 3);   // image stored
+  stamp(2, blockIdx.x, 4);   // image stored
   __syncthreads();
   pdl_launch_dependents();   // k6 may launch now: it waits for this grid's memory before reading the image
 }
@@ -595,8 +603,14 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
     if (tid < GT) s_cnt[tid] = 0;
     pdl_wait();   // k5 complete: image, exact sub-tables and error bands in memory
+    // the image rows valid codes can reach (rows past every live count are never read)
     const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-    for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
+    const int rows = min(256, max(0, __ldcg(p.img_rows + u)));
+    const int per_rb = rows * (Q::COLS * Q::EW / 16);   // 16-byte pieces of one row block
+    for (int i = tid; i < Q::RB * per_rb; i += K6_THREADS) {
+      const int rb = i / per_rb, off = (rb * 256 * 128) / 16 + (i - rb * per_rb);
+      cp_async16(qlut + off * 16, gimg + (int64_t)off * 16);
+    }
     if (tid < GT) s_margin[tid] = __ldcg(p.margin + (int64_t)u * GT + tid);
     cp_async_wait_all();
     __syncthreads();

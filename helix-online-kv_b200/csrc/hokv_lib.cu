@@ -114,8 +114,10 @@ static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
   const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
   if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
+  // an ordinary launch: every cluster of the grid is placed at once on an idle
+  // GPU (a programmatic launch behind k5 left some clusters for a second wave)
   return launch_ex(k6_candidates<CS, GT>, dim3((unsigned)R, (unsigned)(p.B * p.Hkv)), dim3(K6_THREADS), sm, st, p,
-                   "k6_candidates", true, R);
+                   "k6_candidates", false, R);
 }
 
 static int dispatch_stage1(const Cdc03P& p, cudaStream_t st) {
@@ -500,9 +502,9 @@ static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct Plan {
   int n_chunks, chunk, GT, qimg_bytes;
-  size_t cand_key_bytes, cand_cnt_bytes, qimg_total, texact_bytes, margin_bytes;
+  size_t cand_key_bytes, cand_cnt_bytes, qimg_total, texact_bytes, margin_bytes, rows_bytes;
   size_t total() const {
-    return cand_key_bytes + cand_cnt_bytes + qimg_total + texact_bytes + margin_bytes;
+    return cand_key_bytes + cand_cnt_bytes + qimg_total + texact_bytes + margin_bytes + rows_bytes;
   }
 };
 
@@ -558,6 +560,7 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
   pl->qimg_total = a256((size_t)units * pl->qimg_bytes);
   pl->texact_bytes = a256((size_t)units * pl->GT * a->code_bytes * 256 * 4);
   pl->margin_bytes = a256((size_t)units * pl->GT * 4);
+  pl->rows_bytes = a256((size_t)units * 4);
   return HOKV_OK;
 }
 
@@ -590,6 +593,8 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   p.texact = reinterpret_cast<float*>(w);
   w += pl.texact_bytes;
   p.margin = reinterpret_cast<int*>(w);
+  w += pl.margin_bytes;
+  p.img_rows = reinterpret_cast<int*>(w);
   p.qimg_bytes = pl.qimg_bytes;
   p.n_chunks = pl.n_chunks; p.chunk = pl.chunk; p.GT = pl.GT;
   return p;
