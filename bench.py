@@ -862,7 +862,14 @@ def run_phase_stamps(args):
                          "ends_at_median_us": float(np.median(e)), "ends_at_max_us": float(e.max())})
         return rows
 
+    def starts(x):
+        us = np.sort((x[:, 0] - t0) / 1e3)
+        return {"quantiles_us": [float(np.quantile(us, q)) for q in (0, 0.1, 0.25, 0.5, 0.75, 0.9, 1.0)],
+                "histogram_1us": {int(b): int(c) for b, c in zip(*np.unique(np.floor(us).astype(int),
+                                                                              return_counts=True))}}
+
     line = {"metric": "phase stamps (us) of the last layer's decode kernels", "config": config_for(w, 1),
+            "starts": {"k5": starts(k5), "k6": starts(k6), "k7": starts(k7)},
             "k5_ctas": B * H, "k5": table(k5, K5_PHASES), "k6_start_median_us": float(np.median((k6[:, 0] - t0) / 1e3)),
             "k6_ctas": n6, "k6_start_spread_us": float((k6[:, 0].max() - t0) / 1e3), "k6": table(k6, K6_PHASES),
             "k7_ctas": n7, "k7_start_median_us": float(np.median((k7[:, 0] - t0) / 1e3)),

@@ -380,126 +380,134 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
 
 // ===========================================================================
 // K5: the unit's sub-tables and their quantised image, one CTA per
-// (sequence, KV head), K5_THREADS threads.  Thread t takes subspace column
-// s = t % CS and the rows j = t / CS + i * (K5_THREADS / CS) of that column;
-// it loads its live codebook rows straight into registers (every load in
-// flight at once), computes each entry T[g][s][j] = q_g[s] . C_s[j] exactly
-// (reference GEMV order) and stores it into texact[u][g][j][s] (the exact
-// rescoring of k6 and k7 reads it); the per-(head, subspace) ranges are reduced by
-// shuffles and shared atomics, each head gets one quantisation step and error
-// band (quant_scale; the band goes to `margin`), and every quantised entry is
-// written into the unit's image in global memory, which k6 copies into shared
-// memory.  Rows at or past a subspace's live count have the entry 0, padding
-// columns [M, CS) the code 0.
+// (sequence, KV head), K5_THREADS = 512 threads.  Thread t owns codebook row
+// j = t % 256 and the half t / 256 of the subspace columns: it loads its rows
+// C_s[j] straight into registers (every load in flight at once), computes the
+// entries T[g][s][j] = q_g[s] . C_s[j] exactly (reference GEMV order) for the
+// GT query heads and stores them, contiguous per (head, row), into
+// texact[u][g][j][s] (the exact rescoring of k6 and k7 reads it).  The
+// per-(head, subspace) ranges come from one pass over the entries parked in
+// shared memory [g][s][row]; each head gets one quantisation step and error
+// band (quant_scale, the band goes to `margin`); every quantised entry goes to
+// the unit's image in global memory (row j written by its two threads), which
+// k6 copies into shared memory.  Rows at or past a subspace's live count have
+// the entry 0, padding columns [M, CS) the code 0.  Launched programmatically
+// behind the previous kernel: before the wait only L2 prefetches of this
+// CTA's codebook rows, every other access after it.
 // ===========================================================================
 constexpr int K5_THREADS = 512;
 
-constexpr int K5_FIRST_ROWS = 128;   // codebook rows read before the live counts are known
+template <int CS, int GT>
+constexpr size_t k5_smem_bytes(int D) { return (size_t)GT * CS * 256 * 4 + (size_t)GT * D * 4; }
 
 template <int CS, int GT, int SD>
-__device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, float* sq) {
-  constexpr int TPS = K5_THREADS / CS;   // threads per column
-  constexpr int NS = 256 / TPS;          // row slots per thread
-  __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
+__device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, unsigned char* sm) {
+  constexpr int HALF = (CS >= 2) ? CS / 2 : 1;   // subspace columns per thread
   __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
   __shared__ int s_ks[32];
+  float* R = reinterpret_cast<float*>(sm);                         // [GT][CS][256] entries for the ranges
+  float* sq = R + GT * CS * 256;                                   // [GT][D] queries
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int s = tid % CS, r0 = tid / CS;
+  const int j = tid & 255, s0 = (tid >> 8) * HALF;
   const int M = p.M;
-  const float* col = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh + (int64_t)(s < M ? s : 0) * p.slots * SD;
-  const int first = min(p.slots, K5_FIRST_ROWS);
-  // programmatic launch: while the previous kernel drains, only L2 prefetches of
-  // this unit's first codebook rows (a prefetch never reads stale data); every
-  // load and store of this kernel follows the wait
-  if (s < M) {
-    for (int i = 0; i < NS; ++i) {
-      const int j = r0 + i * TPS;
-      if (j < first) asm volatile("prefetch.global.L2 [%0];" ::"l"(col + (int64_t)j * SD));
-    }
+  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+  // before the wait: this thread's codebook rows into L2
+  if (j < p.slots) {
+#pragma unroll
+    for (int c = 0; c < HALF; ++c)
+      if (s0 + c < M) asm volatile("prefetch.global.L2 [%0];" ::"l"(cbase + ((int64_t)(s0 + c) * p.slots + j) * SD));
   }
   pdl_wait();
   stamp(2, blockIdx.x, 1);   // previous kernel complete
-  // every independent load first: live count, the first rows, the queries, the length
-  int ks = 0;
-  if (s < M) ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + s];
-  // rows in registers NB at a time (all of them for sub_dim <= 8)
-  constexpr int NB = (SD <= 8) ? NS : ((64 / SD) < 1 ? 1 : (64 / SD) > NS ? NS : (64 / SD));
-  auto load_rows = [&](int i0, float (&c)[NB][SD], int lo_row, int hi_row) {
+  if (tid < M) {
+    const int kx = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+    s_ks[tid] = kx < 0 ? 0 : (kx > p.slots ? p.slots : kx);
+  }
+  // rows straight into registers, NB columns at a time (all of them for
+  // sub_dim <= 8); slots past `slots` never exist
+  constexpr int NB0 = (SD <= 8) ? HALF : 64 / SD;
+  constexpr int NB = NB0 < 1 ? 1 : (NB0 > HALF ? HALF : NB0);
+  float c[NB][SD];
+  auto load_rows = [&](int c0) {
 #pragma unroll
-    for (int i = 0; i < NB; ++i) {
-      const int j = r0 + (i0 + i) * TPS;
-      if (i0 + i < NS && j >= lo_row && j < hi_row) {
+    for (int cc = 0; cc < NB; ++cc) {
+      if (c0 + cc < HALF && s0 + c0 + cc < M && j < p.slots) {
+        const float* row = cbase + ((int64_t)(s0 + c0 + cc) * p.slots + j) * SD;
 #pragma unroll
         for (int d = 0; d < SD; d += 4) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(col + (int64_t)j * SD + d));
-          c[i][d] = v.x; c[i][d + 1] = v.y; c[i][d + 2] = v.z; c[i][d + 3] = v.w;
+          const float4 v = __ldg(reinterpret_cast<const float4*>(row + d));
+          c[cc][d] = v.x; c[cc][d + 1] = v.y; c[cc][d + 2] = v.z; c[cc][d + 3] = v.w;
         }
       }
     }
   };
-  float c[NB][SD];
-  if (s < M) load_rows(0, c, 0, first);
+  load_rows(0);
   for (int i = tid; i < GT * p.D; i += K5_THREADS) {
     const int g = i / p.D, d = i - g * p.D;
     sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
   }
   const ColdRange cr = cold_range(p, b);
   if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking: k6 and k7 read no table (the same in every thread)
-  ks = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
-  if (s < M && ks > first) load_rows(0, c, first, ks);   // live rows past the first ones (large codebooks)
-  if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
-  if (r0 == 0) s_ks[s] = ks;
   __syncthreads();
   stamp(2, blockIdx.x, 2);   // queries staged
-  float e[NS][GT];
-  unsigned lo[GT], hi[GT];
+  // exact entries of row j, this thread's columns, every head
+  float e[HALF][GT];
+  float* tx = p.texact + ((int64_t)u * GT * 256 + j) * CS;   // + g * 256 * CS + s
 #pragma unroll
-  for (int g = 0; g < GT; ++g) { lo[g] = 0xffffffffu; hi[g] = 0u; }
-  const int64_t tx = (int64_t)u * GT * CS * 256;
+  for (int c0 = 0; c0 < HALF; c0 += NB) {
+    if (c0 > 0) load_rows(c0);
 #pragma unroll
-  for (int i0 = 0; i0 < NS; i0 += NB) {
-    if (i0 > 0 && s < M) load_rows(i0, c, 0, ks);
+    for (int cb = 0; cb < NB; ++cb) {
+      const int cc = c0 + cb;
+      if (cc >= HALF) break;
+      const int sx = s0 + cc;
+      const bool live = sx < M && j < s_ks[sx];
 #pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      float qs[SD];
+      for (int g = 0; g < GT; ++g) {
+        float v = 0.f;
+        if (live) {
+          float qs[SD];
 #pragma unroll
-      for (int d = 0; d < SD; ++d) qs[d] = s < M ? sq[g * p.D + s * SD + d] : 0.f;
-#pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        if (i0 + i < NS) {
-          const int j = r0 + (i0 + i) * TPS;
-          float v = 0.f;
-          if (j < ks) {
-            v = lut_dot2<SD>(qs, c[i]);
-            const unsigned o = ord_f32(v);
-            lo[g] = min(lo[g], o);
-            hi[g] = max(hi[g], o);
-          }
-          e[i0 + i][g] = v;
-          if (j < ks) p.texact[tx + ((int64_t)g * 256 + j) * CS + s] = v;   // live rows only
+          for (int d = 0; d < SD; ++d) qs[d] = sq[g * p.D + sx * SD + d];
+          v = lut_dot2<SD>(qs, c[cb]);
+          tx[(int64_t)g * 256 * CS + sx] = v;   // live entries only
         }
+        e[cc][g] = v;
+        R[(g * CS + sx) * 256 + j] = v;
       }
     }
   }
-  // ranges of each (head, column): lanes of one column, then the warps
-#pragma unroll
-  for (int g = 0; g < GT; ++g) {
-#pragma unroll
-    for (int o = CS; o < 32; o <<= 1) {
-      lo[g] = min(lo[g], __shfl_xor_sync(0xffffffffu, lo[g], o));
-      hi[g] = max(hi[g], __shfl_xor_sync(0xffffffffu, hi[g], o));
-    }
-    if (lane < CS && s < M) { atomicMin(&s_lo[g][s], lo[g]); atomicMax(&s_hi[g][s], hi[g]); }
-  }
   __syncthreads();
-  stamp(2, blockIdx.x, 3);   // entries and ranges
-  if (tid < GT * 32) {
-    const int g = tid / 32, sx = tid % 32;
-    if (sx < M) {
+  stamp(2, blockIdx.x, 3);   // entries
+  // ranges: TPP threads per (head, column) pair, each over 256 / TPP rows
+  {
+    constexpr int PAIRS = GT * CS;
+    constexpr int TPP0 = K5_THREADS / PAIRS;
+    constexpr int TPP = TPP0 > 32 ? 32 : TPP0;
+    constexpr int RPT = 256 / TPP;
+    const int pr = tid / TPP, li = tid % TPP;
+    unsigned lo = 0xffffffffu, hi = 0u;
+    const int g = pr / CS, sx = pr % CS;
+    if (pr < PAIRS && sx < M) {
       const int kx = s_ks[sx];
-      unsigned ol = s_lo[g][sx], oh = s_hi[g][sx];
-      if (kx < 256) { ol = min(ol, ord_f32(0.f)); oh = max(oh, ord_f32(0.f)); }   // zero entries of dead rows
-      float fl = unord_f32(ol), fh = unord_f32(oh);
+      const float* col = R + (g * CS + sx) * 256;
+      for (int r = li * RPT; r < li * RPT + RPT; ++r) {
+        if (r < kx) {
+          const unsigned o = ord_f32(col[r]);
+          lo = min(lo, o);
+          hi = max(hi, o);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < TPP; o <<= 1) {
+      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (li == 0 && pr < PAIRS && sx < M) {
+      const int kx = s_ks[sx];
+      if (kx < 256) { lo = min(lo, ord_f32(0.f)); hi = max(hi, ord_f32(0.f)); }   // zero entries of dead rows
+      float fl = unord_f32(lo), fh = unord_f32(hi);
       if (kx < 256) { fl = fminf(fl, 0.f); fh = fmaxf(fh, 0.f); }
       f_lo[g][sx] = fl;
       f_hi[g][sx] = fh;
@@ -522,28 +530,29 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, fl
   unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
   const int qmax = qmax_for(M);
 #pragma unroll
-  for (int i = 0; i < NS; ++i) {
+  for (int cc = 0; cc < HALF; ++cc) {
+    const int sx = s0 + cc;
     uint32_t code[GT];
 #pragma unroll
-    for (int g = 0; g < GT; ++g) code[g] = (s < M) ? quant_code(e[i][g], f_lo[g][s], s_inv[g], qmax) : 0u;
-    put_entry<CS, GT>(gimg, s, r0 + i * TPS, code);
+    for (int g = 0; g < GT; ++g) code[g] = (sx < M) ? quant_code(e[cc][g], f_lo[g][sx], s_inv[g], qmax) : 0u;
+    put_entry<CS, GT>(gimg, sx, j, code);
   }
   stamp(2, blockIdx.x, 4);   // image stored
   __syncthreads();
-  pdl_launch_dependents();   // k6 may launch now: it waits for this grid's memory before reading the image
+  pdl_launch_dependents();   // the next kernel may launch now
 }
 
 template <int CS, int GT>
 __global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
-  extern __shared__ __align__(16) float k5_sq[];   // [GT][D] queries
+  extern __shared__ __align__(16) unsigned char k5_sm[];   // ranges [GT][CS][256], queries [GT][D]
   stamp(2, blockIdx.x, 0);
   const int u = blockIdx.x;
   const int b = u / p.Hkv, h = u - b * p.Hkv;
   switch (p.sd) {
-    case 4: k5_body<CS, GT, 4>(p, u, b, h, k5_sq); break;
-    case 8: k5_body<CS, GT, 8>(p, u, b, h, k5_sq); break;
-    case 16: k5_body<CS, GT, 16>(p, u, b, h, k5_sq); break;
-    case 32: k5_body<CS, GT, 32>(p, u, b, h, k5_sq); break;
+    case 4: k5_body<CS, GT, 4>(p, u, b, h, k5_sm); break;
+    case 8: k5_body<CS, GT, 8>(p, u, b, h, k5_sm); break;
+    case 16: k5_body<CS, GT, 16>(p, u, b, h, k5_sm); break;
+    case 32: k5_body<CS, GT, 32>(p, u, b, h, k5_sm); break;
     default: dev_flag(HOKV_ERR_DEVICE_INPUT);
   }
 }

@@ -106,7 +106,7 @@ template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
-  const size_t sm5 = (size_t)GT * p.D * 4;   // queries
+  const size_t sm5 = k5_smem_bytes<CS, GT>(p.D);   // entries for the ranges, queries
   if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
   if (int e = launch_ex(k5_tables<CS, GT>, dim3((unsigned)(p.B * p.Hkv)), dim3(K5_THREADS), sm5, st, p,
                         "k5_tables", true))
