@@ -397,16 +397,27 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
 // ===========================================================================
 constexpr int K5_THREADS = 512;
 
+// Threads per (head, column) pair in k5's range pass, and the padded row
+// stride of its entry table: with stride 256 + TPP the TPP threads of a pair
+// (consecutive rows) and the pairs of one warp hit distinct banks.
 template <int CS, int GT>
-constexpr size_t k5_smem_bytes(int D) { return (size_t)GT * CS * 256 * 4 + (size_t)GT * D * 4; }
+struct K5Geo {
+  static constexpr int PAIRS = GT * CS;
+  static constexpr int TPP0 = K5_THREADS / PAIRS;
+  static constexpr int TPP = TPP0 > 32 ? 32 : TPP0;
+  static constexpr int RS = 256 + TPP;
+};
+template <int CS, int GT>
+constexpr size_t k5_smem_bytes(int D) { return (size_t)GT * CS * K5Geo<CS, GT>::RS * 4 + (size_t)GT * D * 4; }
 
 template <int CS, int GT, int SD>
 __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, unsigned char* sm) {
   constexpr int HALF = (CS >= 2) ? CS / 2 : 1;   // subspace columns per thread
   __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
   __shared__ int s_ks[32];
-  float* R = reinterpret_cast<float*>(sm);                         // [GT][CS][256] entries for the ranges
-  float* sq = R + GT * CS * 256;                                   // [GT][D] queries
+  using KG = K5Geo<CS, GT>;
+  float* R = reinterpret_cast<float*>(sm);                         // [GT * CS][RS] entries for the ranges
+  float* sq = R + GT * CS * KG::RS;                                // [GT][D] queries
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int j = tid & 255, s0 = (tid >> 8) * HALF;
   const int M = p.M;
@@ -473,30 +484,25 @@ __device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, un
           tx[(int64_t)g * 256 * CS + sx] = v;   // live entries only
         }
         e[cc][g] = v;
-        R[(g * CS + sx) * 256 + j] = v;
+        R[(g * CS + sx) * KG::RS + j] = v;
       }
     }
   }
   __syncthreads();
   stamp(2, blockIdx.x, 3);   // entries
-  // ranges: TPP threads per (head, column) pair, each over 256 / TPP rows
+  // ranges: TPP threads per (head, column) pair, rows li, li + TPP, ...
   {
-    constexpr int PAIRS = GT * CS;
-    constexpr int TPP0 = K5_THREADS / PAIRS;
-    constexpr int TPP = TPP0 > 32 ? 32 : TPP0;
-    constexpr int RPT = 256 / TPP;
+    constexpr int PAIRS = KG::PAIRS, TPP = KG::TPP;
     const int pr = tid / TPP, li = tid % TPP;
     unsigned lo = 0xffffffffu, hi = 0u;
     const int g = pr / CS, sx = pr % CS;
     if (pr < PAIRS && sx < M) {
       const int kx = s_ks[sx];
-      const float* col = R + (g * CS + sx) * 256;
-      for (int r = li * RPT; r < li * RPT + RPT; ++r) {
-        if (r < kx) {
-          const unsigned o = ord_f32(col[r]);
-          lo = min(lo, o);
-          hi = max(hi, o);
-        }
+      const float* col = R + (g * CS + sx) * KG::RS;
+      for (int r = li; r < kx; r += TPP) {
+        const unsigned o = ord_f32(col[r]);
+        lo = min(lo, o);
+        hi = max(hi, o);
       }
     }
 #pragma unroll
