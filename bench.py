@@ -658,7 +658,7 @@ def run_ours(args):
     peak, peak_kind = _peaks()
     k6_gbs = k6_bytes / (k6_ms * 1e-3) / 1e9
     k7_gbs = k7_bytes / (k7_ms * 1e-3) / 1e9
-    s1 = ("k5_tables + k6_candidates (candidate stage)", k6_gbs, k6_bytes, k6_ms)
+    s1 = ("k6_candidates (tables built in thread-block clusters)", k6_gbs, k6_bytes, k6_ms)
     s2 = ("k7_select_attend", k7_gbs, k7_bytes, k7_ms)
     dom, other = (s1, s2) if k6_ms >= k7_ms else (s2, s1)
 
@@ -790,7 +790,7 @@ def run_ours(args):
         "vq_assign": {"value": as_gbs, "unit": "GB/s", "frac": as_gbs / peak, "vectors": units * n_new,
                       "ms": as_ms, "kernel": "k_pq_assign_tc (tcgen05 tf32 screen into tensor memory, exact fp32 "
                                              "rescoring of the candidates)"},
-        "gpu_launches": args.steps * Ls * 3,   # k5_tables + k6_candidates + k7_select_attend per layer
+        "gpu_launches": args.steps * Ls * 2,   # k6_candidates + k7_select_attend per layer
         "check": check,
         "clocks": clk.summary(),
         "setup_s": t_setup,
@@ -805,9 +805,8 @@ def run_ours(args):
     return 0
 
 
-K6_PHASES = ["wait for k5 + image to smem", "score own chunks", "pool histograms", "threshold", "list+rescore"]
-K5_PHASES = ["prefetch + wait for the previous kernel", "queries staged (rows in flight)", "entries + ranges",
-             "image stored"]
+K6_PHASES = ["rows+queries staged", "dots", "ranges exchanged", "own image entries", "cluster image barrier",
+             "image to smem", "score own chunks", "pool histograms", "threshold", "list+rescore"]
 K7_PHASES = ["hot window", "wait for k6", "selection", "attend selected", "combine+store"]
 
 
@@ -848,10 +847,9 @@ def run_phase_stamps(args):
     st = buf.reshape(3, 4096, 16).astype(np.int64)
     n6 = min(B * H * 8, 4096)
     n7 = B * Hq
-    k5 = st[2, :B * H, :len(K5_PHASES) + 1]
     k6 = st[0, :n6, :len(K6_PHASES) + 1]
     k7 = st[1, :n7, :len(K7_PHASES) + 1]
-    t0 = int(min(k5[:, 0].min(), k6[:, 0].min()))
+    t0 = int(k6[:, 0].min())
 
     def table(x, names):
         rows = []
@@ -869,8 +867,7 @@ def run_phase_stamps(args):
                                                                               return_counts=True))}}
 
     line = {"metric": "phase stamps (us) of the last layer's decode kernels", "config": config_for(w, 1),
-            "starts": {"k5": starts(k5), "k6": starts(k6), "k7": starts(k7)},
-            "k5_ctas": B * H, "k5": table(k5, K5_PHASES), "k6_start_median_us": float(np.median((k6[:, 0] - t0) / 1e3)),
+            "starts": {"k6": starts(k6), "k7": starts(k7)},
             "k6_ctas": n6, "k6_start_spread_us": float((k6[:, 0].max() - t0) / 1e3), "k6": table(k6, K6_PHASES),
             "k7_ctas": n7, "k7_start_median_us": float(np.median((k7[:, 0] - t0) / 1e3)),
             "k7_start_max_us": float((k7[:, 0].max() - t0) / 1e3), "k7": table(k7, K7_PHASES),

@@ -1,20 +1,17 @@
 // cdc03.cuh -- PQ lookup tables, ADC scoring and CDC-03 decode attention.
 //
-// Decode step, per layer, three kernels chained with programmatic dependent
-// launch (K6 prefetches its codes while K5 runs; K7 starts its hot-window
-// attention while K6 runs):
-//   K5 k5_tables  grid (B*H_kv), one CTA per (sequence, KV head): the exact
-//      fp32 sub-tables T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads
-//      of the GQA group (BLAS order) and their quantised image (codes of
-//      floor(65535 / M) levels in 16-bit lanes, laid out so every
-//      shared-memory lookup of K6 is bank-conflict free).
+// Decode step, per layer, two kernels chained with programmatic dependent
+// launch (K7 starts its hot-window attention while K6 runs):
 //   K6 k6_candidates  grid (min(chunks, 8), B*H_kv), one thread-block cluster
-//      per (sequence, KV head): each CTA copies the image into shared memory,
-//      streams the uint8 PQ codes of its 2048-token chunks into registers,
-//      sums quantised entries per token in integer lanes, pools a score
-//      histogram over the cluster, and emits every token whose score lies
-//      within the proven error band of the unit's k'-th score, rescored
-//      exactly (reference summation order) into a selection key.
+//      per (sequence, KV head): the CTAs build the exact fp32 sub-tables
+//      T[g][s][j] = q_g[s-slice] . C_s[j] of the G query heads of the GQA
+//      group (BLAS order) and their quantised image (codes of floor(65535 / M)
+//      levels in 16-bit lanes, laid out so every shared-memory lookup is bank
+//      conflict free); each CTA streams the uint8 PQ codes of its 2048-token
+//      chunks into registers, sums quantised entries per token in integer
+//      lanes, pools a score histogram over the cluster, and emits every token
+//      whose score lies within the proven error band of the unit's k'-th
+//      score, rescored exactly (reference summation order) into a selection key.
 //   K7 k7_select_attend  grid (B*H_kv*G): attends the hot window before it
 //      waits for K6, selects sinks + top-(k - sinks) of the candidate keys
 //      (ties to the lower token index) and finishes softmax attention over them.
@@ -30,6 +27,7 @@
 namespace hokv {
 
 constexpr int K6_THREADS = 256;
+constexpr int K6_FIRST_ROWS = 128;  // codebook rows per subspace staged before the live counts are read
 
 constexpr int CAND_MAX = 512;        // candidates per (unit, chunk, head)
 constexpr int K7_THREADS = 256;
@@ -57,9 +55,8 @@ struct Cdc03P {
   uint64_t* cand_key;     // [units][chunks][GT][CAND_MAX] selection keys of listed candidates (K6 -> K7)
   int* cand_cnt;          // [units][chunks][GT]   listed count, -1 when the list overflowed
   unsigned char* qimg;    // [units][qimg_bytes]     quantised sub-table images (exchanged in the cluster)
-  float* texact;          // [units][GT][256][CS]    exact sub-tables (K6 rescoring, K7 rescans)
+  float* texact;          // [units][GT][CS][256]    exact sub-tables (K6 rescoring, K7 rescans)
   int* margin;            // [units][GT]             error band in code units
-  int* img_rows;          // [units]                 image rows k6 copies (the largest live count)
   int n_chunks, chunk, GT, qimg_bytes;
 };
 
@@ -165,10 +162,25 @@ __device__ __forceinline__ void rotate_bytes(uint32_t (&w)[W], int r) {
 }
 
 // Exact sub-table entry: the GEMV order of NumPy/OpenBLAS for (1 x SD) @ (SD x k)
-// (hokv_math.cuh), so the value equals the reference's bit for bit.
+// (hokv_math.cuh dot_gemv), so the value equals the reference's bit for bit;
+// the paired products and sums of the 4- and 8-dim orders run as fp32x2
+// operations, which round each lane as its scalar twin does.
 template <int SD>
 __device__ __forceinline__ float lut_dot(const float* q, const float* c) {
-  return dot_gemv(q, c, SD);
+  if constexpr (SD == 4) {
+    const float2 a = __fmul2_rn(make_float2(q[0], q[2]), make_float2(c[0], c[2]));
+    const float2 b = __fmul2_rn(make_float2(q[1], q[3]), make_float2(c[1], c[3]));
+    const float2 s = __fadd2_rn(a, b);   // {p0 + p1, p2 + p3}
+    return fadd(s.x, s.y);
+  } else if constexpr (SD == 8) {
+    float2 pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = __fmul2_rn(make_float2(q[i], q[i + 4]), make_float2(c[i], c[i + 4]));
+    const float2 s = __fadd2_rn(__fadd2_rn(pr[0], pr[1]), __fadd2_rn(pr[2], pr[3]));
+    return fadd(s.x, s.y);   // ((p0+p1)+(p2+p3)) + ((p4+p5)+(p6+p7))
+  } else {
+    return dot_gemv(q, c, SD);
+  }
 }
 
 // Quantisation of one head's tables from the per-subspace ranges [lo, hi]
@@ -233,8 +245,10 @@ __device__ __forceinline__ uint16_t quant_code(float t, float lo, float inv, int
 // ===========================================================================
 // K6: candidate stream, grid (min(chunks, 8), B*H_kv), 256 threads, 8 tokens
 // of a 2048-token chunk per thread.  The CTAs of one (b, KV head) form a
-// thread-block cluster that pools its score histograms, so the threshold is
-// the unit-wide k'-th score at any context length; the tables come from K5.
+// thread-block cluster that builds the unit's tables itself (each CTA one
+// block of subspaces; ranges exchanged through distributed shared memory, the
+// quantised image through L2) and pools its score histograms, so the
+// threshold is the unit-wide k'-th score at any context length.
 // ===========================================================================
 constexpr int K6_TPT = 8;
 constexpr int K6_CHUNK = K6_THREADS * K6_TPT;   // 2048 tokens
@@ -333,25 +347,42 @@ __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane)
 template <int CS, int GT>
 constexpr int k6_min_blocks() { return ((GT == 8 && CS >= 16) || (CS == 32 && GT >= 4)) ? 3 : 4; }
 
-// Exact sub-table entry T = q . c for one codebook row: the reference GEMV
-// order (hokv_math.cuh dot_gemv) with the paired products and sums of the
-// 4- and 8-dim orders in fp32x2 operations, which round each lane as its
-// scalar twin does.
-template <int SD>
-__device__ __forceinline__ float lut_dot2(const float* q, const float* c) {
-  if constexpr (SD == 4) {
-    const float2 a = __fmul2_rn(make_float2(q[0], q[2]), make_float2(c[0], c[2]));
-    const float2 b = __fmul2_rn(make_float2(q[1], q[3]), make_float2(c[1], c[3]));
-    const float2 s = __fadd2_rn(a, b);   // {p0 + p1, p2 + p3}
-    return fadd(s.x, s.y);
-  } else if constexpr (SD == 8) {
-    float2 pr[4];
+// Dot phase of the in-cluster table build: thread j computes entry j of the
+// subspaces [s_begin, s_end) for the GT query heads of the group, stores the
+// exact fp32 value (for the exact rescoring), folds it into the
+// per-(head, subspace) range and keeps the first two subspaces' values in
+// registers for the quantisation.  Row (s, j) of the codebook is at
+// rows + ((s - s_off) * slots + j) * SD.
+template <int GT, int SD>
+__device__ __forceinline__ void lut_dot_row(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
+                                            const int* s_k, int s, unsigned (*s_lo)[32], unsigned (*s_hi)[32],
+                                            float (&tv)[GT]) {
+  const int j = threadIdx.x, lane = j & 31;
+  const bool live = j < s_k[s];
+  float c[SD];
+  const float* row = rows + ((int64_t)(s - s_off) * p.slots + j) * SD;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pr[i] = __fmul2_rn(make_float2(q[i], q[i + 4]), make_float2(c[i], c[i + 4]));
-    const float2 s = __fadd2_rn(__fadd2_rn(pr[0], pr[1]), __fadd2_rn(pr[2], pr[3]));
-    return fadd(s.x, s.y);   // ((p0+p1)+(p2+p3)) + ((p4+p5)+(p6+p7))
-  } else {
-    return dot_gemv(q, c, SD);
+  for (int d = 0; d < SD; ++d) c[d] = live ? row[d] : 0.f;
+#pragma unroll
+  for (int g = 0; g < GT; ++g) {
+    const float t = live ? lut_dot<SD>(sq + g * p.D + s * SD, c) : 0.f;
+    tv[g] = t;
+    p.texact[(((int64_t)u * GT + g) * p.CS + s) * 256 + j] = t;
+    const unsigned o = ord_f32(t);
+    const unsigned mn = __reduce_min_sync(0xffffffffu, o), mx = __reduce_max_sync(0xffffffffu, o);
+    if (lane == 0) { atomicMin(&s_lo[g][s], mn); atomicMax(&s_hi[g][s], mx); }
+  }
+}
+
+template <int GT, int SD>
+__device__ __forceinline__ void lut_dots(const Cdc03P& p, int u, const float* rows, int s_off, const float* sq,
+                                         const int* s_k, int s_begin, int s_end, unsigned (*s_lo)[32],
+                                         unsigned (*s_hi)[32], float (&tv)[2][GT]) {
+  if (s_begin < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin, s_lo, s_hi, tv[0]);
+  if (s_begin + 1 < s_end) lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s_begin + 1, s_lo, s_hi, tv[1]);
+  for (int s = s_begin + 2; s < s_end; ++s) {
+    float tmp[GT];
+    lut_dot_row<GT, SD>(p, u, rows, s_off, sq, s_k, s, s_lo, s_hi, tmp);
   }
 }
 
@@ -375,191 +406,6 @@ __device__ __forceinline__ void put_entry(unsigned char* img, int sx, int j, con
     if constexpr (Q::EW == 4) reinterpret_cast<uint32_t*>(img)[e] = e32[0];
     else if constexpr (Q::EW == 8) reinterpret_cast<uint2*>(img)[e] = make_uint2(e32[0], e32[1]);
     else reinterpret_cast<uint4*>(img)[e] = make_uint4(e32[0], e32[1], e32[2], e32[3]);
-  }
-}
-
-// ===========================================================================
-// K5: the unit's sub-tables and their quantised image, one CTA per
-// (sequence, KV head), K5_THREADS = 512 threads.  Thread t owns codebook row
-// j = t % 256 and the half t / 256 of the subspace columns: it loads its rows
-// C_s[j] straight into registers (every load in flight at once), computes the
-// entries T[g][s][j] = q_g[s] . C_s[j] exactly (reference GEMV order) for the
-// GT query heads and stores them, contiguous per (head, row), into
-// texact[u][g][j][s] (the exact rescoring of k6 and k7 reads it).  The
-// per-(head, subspace) ranges come from one pass over the entries parked in
-// shared memory [g][s][row]; each head gets one quantisation step and error
-// band (quant_scale, the band goes to `margin`); every quantised entry goes to
-// the unit's image in global memory (row j written by its two threads), which
-// k6 copies into shared memory.  Rows at or past a subspace's live count have
-// the entry 0, padding columns [M, CS) the code 0.  Launched programmatically
-// behind the previous kernel: before the wait only L2 prefetches of this
-// CTA's codebook rows, every other access after it.
-// ===========================================================================
-constexpr int K5_THREADS = 512;
-
-// Threads per (head, column) pair in k5's range pass, and the padded row
-// stride of its entry table: with stride 256 + TPP the TPP threads of a pair
-// (consecutive rows) and the pairs of one warp hit distinct banks.
-template <int CS, int GT>
-struct K5Geo {
-  static constexpr int PAIRS = GT * CS;
-  static constexpr int TPP0 = K5_THREADS / PAIRS;
-  static constexpr int TPP = TPP0 > 32 ? 32 : TPP0;
-  static constexpr int RS = 256 + TPP;
-};
-template <int CS, int GT>
-constexpr size_t k5_smem_bytes(int D) { return (size_t)GT * CS * K5Geo<CS, GT>::RS * 4 + (size_t)GT * D * 4; }
-
-template <int CS, int GT, int SD>
-__device__ __forceinline__ void k5_body(const Cdc03P& p, int u, int b, int h, unsigned char* sm) {
-  constexpr int HALF = (CS >= 2) ? CS / 2 : 1;   // subspace columns per thread
-  __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
-  __shared__ int s_ks[32];
-  using KG = K5Geo<CS, GT>;
-  float* R = reinterpret_cast<float*>(sm);                         // [GT * CS][RS] entries for the ranges
-  float* sq = R + GT * CS * KG::RS;                                // [GT][D] queries
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int j = tid & 255, s0 = (tid >> 8) * HALF;
-  const int M = p.M;
-  const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
-  // before the wait: this thread's codebook rows into L2
-  if (j < p.slots) {
-#pragma unroll
-    for (int c = 0; c < HALF; ++c)
-      if (s0 + c < M) asm volatile("prefetch.global.L2 [%0];" ::"l"(cbase + ((int64_t)(s0 + c) * p.slots + j) * SD));
-  }
-  pdl_wait();
-  stamp(2, blockIdx.x, 1);   // previous kernel complete
-  if (tid < M) {
-    const int kx = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
-    s_ks[tid] = kx < 0 ? 0 : (kx > p.slots ? p.slots : kx);
-  }
-  // rows straight into registers, NB columns at a time (all of them for
-  // sub_dim <= 8); slots past `slots` never exist
-  constexpr int NB0 = (SD <= 8) ? HALF : 64 / SD;
-  constexpr int NB = NB0 < 1 ? 1 : (NB0 > HALF ? HALF : NB0);
-  float c[NB][SD];
-  auto load_rows = [&](int c0) {
-#pragma unroll
-    for (int cc = 0; cc < NB; ++cc) {
-      if (c0 + cc < HALF && s0 + c0 + cc < M && j < p.slots) {
-        const float* row = cbase + ((int64_t)(s0 + c0 + cc) * p.slots + j) * SD;
-#pragma unroll
-        for (int d = 0; d < SD; d += 4) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(row + d));
-          c[cc][d] = v.x; c[cc][d + 1] = v.y; c[cc][d + 2] = v.z; c[cc][d + 3] = v.w;
-        }
-      }
-    }
-  };
-  load_rows(0);
-  for (int i = tid; i < GT * p.D; i += K5_THREADS) {
-    const int g = i / p.D, d = i - g * p.D;
-    sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
-  }
-  const ColdRange cr = cold_range(p, b);
-  if (cr.k >= cr.Sc || cr.kp <= 0) return;   // no ranking: k6 and k7 read no table (the same in every thread)
-  __syncthreads();
-  stamp(2, blockIdx.x, 2);   // queries staged
-  // exact entries of row j, this thread's columns, every head
-  float e[HALF][GT];
-  float* tx = p.texact + ((int64_t)u * GT * 256 + j) * CS;   // + g * 256 * CS + s
-#pragma unroll
-  for (int c0 = 0; c0 < HALF; c0 += NB) {
-    if (c0 > 0) load_rows(c0);
-#pragma unroll
-    for (int cb = 0; cb < NB; ++cb) {
-      const int cc = c0 + cb;
-      if (cc >= HALF) break;
-      const int sx = s0 + cc;
-      const bool live = sx < M && j < s_ks[sx];
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float v = 0.f;
-        if (live) {
-          float qs[SD];
-#pragma unroll
-          for (int d = 0; d < SD; ++d) qs[d] = sq[g * p.D + sx * SD + d];
-          v = lut_dot2<SD>(qs, c[cb]);
-          tx[(int64_t)g * 256 * CS + sx] = v;   // live entries only
-        }
-        e[cc][g] = v;
-        R[(g * CS + sx) * KG::RS + j] = v;
-      }
-    }
-  }
-  __syncthreads();
-  stamp(2, blockIdx.x, 3);   // entries
-  // ranges: TPP threads per (head, column) pair, rows li, li + TPP, ...
-  {
-    constexpr int PAIRS = KG::PAIRS, TPP = KG::TPP;
-    const int pr = tid / TPP, li = tid % TPP;
-    unsigned lo = 0xffffffffu, hi = 0u;
-    const int g = pr / CS, sx = pr % CS;
-    if (pr < PAIRS && sx < M) {
-      const int kx = s_ks[sx];
-      const float* col = R + (g * CS + sx) * KG::RS;
-      for (int r = li; r < kx; r += TPP) {
-        const unsigned o = ord_f32(col[r]);
-        lo = min(lo, o);
-        hi = max(hi, o);
-      }
-    }
-#pragma unroll
-    for (int o = 1; o < TPP; o <<= 1) {
-      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-    }
-    if (li == 0 && pr < PAIRS && sx < M) {
-      const int kx = s_ks[sx];
-      if (kx < 256) { lo = min(lo, ord_f32(0.f)); hi = max(hi, ord_f32(0.f)); }   // zero entries of dead rows
-      float fl = unord_f32(lo), fh = unord_f32(hi);
-      if (kx < 256) { fl = fminf(fl, 0.f); fh = fmaxf(fh, 0.f); }
-      f_lo[g][sx] = fl;
-      f_hi[g][sx] = fh;
-    }
-  }
-  __syncthreads();
-  if (warp < GT) {   // one warp per head
-    const QuantScale qsc = quant_scale_warp(f_lo[warp], f_hi[warp], M, p.scale, lane);
-    if (lane == 0) {
-      s_inv[warp] = qsc.inv;
-      p.margin[(int64_t)u * GT + warp] = qsc.margin;
-    }
-  } else if (warp == GT) {   // the image rows valid codes can reach: the largest live count
-    int kx = lane < M ? s_ks[lane] : 0;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) kx = max(kx, __shfl_xor_sync(0xffffffffu, kx, o));
-    if (lane == 0) p.img_rows[u] = kx;
-  }
-  __syncthreads();
-  unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-  const int qmax = qmax_for(M);
-#pragma unroll
-  for (int cc = 0; cc < HALF; ++cc) {
-    const int sx = s0 + cc;
-    uint32_t code[GT];
-#pragma unroll
-    for (int g = 0; g < GT; ++g) code[g] = (sx < M) ? quant_code(e[cc][g], f_lo[g][sx], s_inv[g], qmax) : 0u;
-    put_entry<CS, GT>(gimg, sx, j, code);
-  }
-  stamp(2, blockIdx.x, 4);   // image stored
-  __syncthreads();
-  pdl_launch_dependents();   // the next kernel may launch now
-}
-
-template <int CS, int GT>
-__global__ void __launch_bounds__(K5_THREADS, 1) k5_tables(Cdc03P p) {
-  extern __shared__ __align__(16) unsigned char k5_sm[];   // ranges [GT][CS][256], queries [GT][D]
-  stamp(2, blockIdx.x, 0);
-  const int u = blockIdx.x;
-  const int b = u / p.Hkv, h = u - b * p.Hkv;
-  switch (p.sd) {
-    case 4: k5_body<CS, GT, 4>(p, u, b, h, k5_sm); break;
-    case 8: k5_body<CS, GT, 8>(p, u, b, h, k5_sm); break;
-    case 16: k5_body<CS, GT, 16>(p, u, b, h, k5_sm); break;
-    case 32: k5_body<CS, GT, 32>(p, u, b, h, k5_sm); break;
-    default: dev_flag(HOKV_ERR_DEVICE_INPUT);
   }
 }
 
@@ -598,16 +444,142 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   uint32_t w[HT][Q::W];
   const int c0 = me;
   {
-    // ---- codes of this CTA into L2 and its first half-chunk into registers,
-    // then the unit's tables from k5 (programmatic launch: k5 may still run)
+    // ---- tables built by the cluster: each CTA computes a block of subspaces
+    // (whole 16-byte groups of the image), the ranges go to every CTA through
+    // distributed shared memory, the quantised entries to the unit's image in
+    // global memory, from where every CTA loads the whole image
+    __shared__ unsigned s_lo[GT][32], s_hi[GT][32];
+    __shared__ float f_lo[GT][32], f_hi[GT][32], s_inv[GT];
+    __shared__ int s_k[32];
+    cluster_arrive_relaxed();   // phase A: this CTA runs
+    constexpr int GS = 16 / Q::EW;                 // subspaces per 16-byte group
+    const int ngm = (M + GS - 1) / GS;             // groups holding real subspaces
+    const int grp0 = me * ngm / R, grp1 = (me + 1) * ngm / R;
+    const int s_begin = grp0 * GS, s_end = min(grp1 * GS, M);
+    const float* cbase = p.cb + (int64_t)b * p.cb_sb + (int64_t)h * p.cb_sh;
+    // own codebook rows into shared memory (the image space is free until the
+    // image is loaded), with the queries: the first K6_FIRST_ROWS rows of each
+    // subspace now, the live rows past them (if any) once the counts are known
+    const int64_t per_s = (int64_t)p.slots * p.sd;                           // floats per subspace
+    const int64_t blk = (int64_t)max(0, s_end - s_begin) * per_s;
+    const bool staged = blk * 4 <= Q::BYTES;
+    const float* src = cbase + (int64_t)s_begin * per_s;
+    const int first = min(p.slots, K6_FIRST_ROWS);
+    const int row16 = p.sd / 4;                                              // 16-byte pieces per row
+    if (staged) {   // 32-bit index math: a staged block holds at most Q::BYTES
+      const int per_sub = first * row16;
+      const int n16 = (s_end - s_begin) * per_sub;
+      for (int i = tid; i < n16; i += K6_THREADS) {
+        const int sr = i / per_sub;
+        const int off = sr * (int)per_s + (i - sr * per_sub) * 4;
+        cp_async16(qlut + off * 4, src + off);
+      }
+    }
+    float* sq = reinterpret_cast<float*>(hist);   // [GT][D], dead before the histograms
+    for (int i = tid; i < GT * p.D; i += K6_THREADS) {
+      const int g = i / p.D, d = i - g * p.D;
+      sq[i] = g < p.G ? load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)(h * p.G + g) * p.D + d) : 0.f;
+    }
+    if (tid < M) {
+      const int ks = p.cbk[(int64_t)b * p.cbk_sb + (int64_t)h * p.cbk_sh + tid];
+      s_k[tid] = ks < 0 ? 0 : (ks > p.slots ? p.slots : ks);
+    }
+    if (tid < GT * 32) { s_lo[tid / 32][tid % 32] = 0xffffffffu; s_hi[tid / 32][tid % 32] = 0u; }
+    cp_async_wait_all();
+    __syncthreads();
+    stamp(0, scta, 1);   // codebook rows and queries staged
+    if (staged && p.slots > first) {
+      bool more = false;   // the same in every thread: the counts are in shared memory
+      for (int sx = s_begin; sx < s_end; ++sx) more |= s_k[sx] > first;
+      if (more) {
+        for (int sx = s_begin; sx < s_end; ++sx) {
+          const int64_t base = (int64_t)(sx - s_begin) * per_s + (int64_t)first * p.sd;
+          const int64_t n16 = (int64_t)max(0, s_k[sx] - first) * row16;
+          for (int64_t i = tid; i < n16; i += K6_THREADS) cp_async16(qlut + (base + i * 4) * 4, src + base + i * 4);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+      }
+    }
+    float tv[2][GT];
+    const float* rows = staged ? reinterpret_cast<const float*>(qlut) : cbase;
+    const int s_off = staged ? s_begin : 0;
+    switch (p.sd) {
+      case 4: lut_dots<GT, 4>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 8: lut_dots<GT, 8>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 16: lut_dots<GT, 16>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      case 32: lut_dots<GT, 32>(p, u, rows, s_off, sq, s_k, s_begin, s_end, s_lo, s_hi, tv); break;
+      default: dev_flag(HOKV_ERR_DEVICE_INPUT);
+    }
+    // this CTA's codes into L2 while the cluster exchanges and quantises the
+    // tables (issued after the table reads, which are on the critical path)
     for (int i = 0; i < n_mine; ++i) {
       const int t0 = (me + i * R) * K6_CHUNK;
       const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
       for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
     }
+    __syncthreads();
+    stamp(0, scta, 2);   // dots done
+    cluster_wait();             // phase A: every CTA of the cluster runs
+    if (tid < GT * 32) {        // own ranges into every CTA
+      const int g = tid / 32, sx = tid % 32;
+      if (sx >= s_begin && sx < s_end) {
+        float lo = unord_f32(s_lo[g][sx]), hi = unord_f32(s_hi[g][sx]);
+        if (s_k[sx] < 256) { lo = fminf(lo, 0.f); hi = fmaxf(hi, 0.f); }   // zero-padded entries
+        for (int rk = 0; rk < R; ++rk) {
+          cl.map_shared_rank(&f_lo[0][0], (unsigned)rk)[g * 32 + sx] = lo;
+          cl.map_shared_rank(&f_hi[0][0], (unsigned)rk)[g * 32 + sx] = hi;
+        }
+      }
+    }
+    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
+    if (tid < GT) s_cnt[tid] = 0;
+    cluster_arrive();
+    cluster_wait();             // phase B: all ranges in every CTA
+    stamp(0, scta, 3);   // ranges exchanged
+    if (warp < GT) {   // one warp per head
+      const QuantScale qs = quant_scale_warp(f_lo[warp], f_hi[warp], M, p.scale, lane);
+      if (lane == 0) {
+        s_inv[warp] = qs.inv;
+        s_margin[warp] = qs.margin;
+        if (me == 0) p.margin[(int64_t)u * GT + warp] = qs.margin;
+      }
+    }
+    __syncthreads();
+    unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
+    {
+      const int qmax = qmax_for(M), j = tid;
+      uint32_t code[GT];
 #pragma unroll
-    for (int it = 0; it < HT; ++it) {
+      for (int kk = 0; kk < 2; ++kk) {
+        const int sx = s_begin + kk;
+        if (sx < s_end) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) code[g] = quant_code(tv[kk][g], f_lo[g][sx], s_inv[g], qmax);
+          put_entry<CS, GT>(gimg, sx, j, code);
+        }
+      }
+      for (int sx = s_begin + 2; sx < s_end; ++sx) {
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+          code[g] = quant_code(p.texact[(((int64_t)u * GT + g) * CS + sx) * 256 + j], f_lo[g][sx], s_inv[g], qmax);
+        put_entry<CS, GT>(gimg, sx, j, code);
+      }
+      // padding subspaces [M, CS): zero entries, written by the owner of the
+      // group (rank 0 for groups without a real subspace)
+#pragma unroll
+      for (int g = 0; g < GT; ++g) code[g] = 0u;
+      for (int sx = M; sx < CS; ++sx) {
+        const int grp = sx / GS;
+        const int own = grp < ngm ? ((grp + 1) * R - 1) / ngm : 0;
+        if (own == me) put_entry<CS, GT>(gimg, sx, j, code);
+      }
+    }
+    stamp(0, scta, 4);   // own image entries written
+    cluster_arrive();           // phase C: the image is complete in memory
+#pragma unroll
+    for (int it = 0; it < HT; ++it) {   // first codes of the first chunk meanwhile
       const int t = c0 * K6_CHUNK + it * K6_THREADS + tid;
       if (t < cr.Sc) load_code<Q::W>(gcodes + (int64_t)t * CS, w[it]);
       else {
@@ -615,21 +587,12 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         for (int i = 0; i < Q::W; ++i) w[it][i] = 0;
       }
     }
-    for (int i = tid; i < GT * HWORDS; i += K6_THREADS) hist[i] = 0;
-    if (tid < GT) s_cnt[tid] = 0;
-    pdl_wait();   // k5 complete: image, exact sub-tables and error bands in memory
-    // the image rows valid codes can reach (rows past every live count are never read)
-    const unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
-    const int rows = min(256, max(0, __ldcg(p.img_rows + u)));
-    const int per_rb = rows * (Q::COLS * Q::EW / 16);   // 16-byte pieces of one row block
-    for (int i = tid; i < Q::RB * per_rb; i += K6_THREADS) {
-      const int rb = i / per_rb, off = (rb * 256 * 128) / 16 + (i - rb * per_rb);
-      cp_async16(qlut + off * 16, gimg + (int64_t)off * 16);
-    }
-    if (tid < GT) s_margin[tid] = __ldcg(p.margin + (int64_t)u * GT + tid);
+    cluster_wait();
+    stamp(0, scta, 5);   // every CTA's image entries written
+    for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
     cp_async_wait_all();
     __syncthreads();
-    stamp(0, scta, 1);   // image in shared memory
+    stamp(0, scta, 6);   // image in shared memory
   }
 
   // ---- quantised scores of one chunk, kept in registers ----------------------
@@ -771,10 +734,10 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       const uint32_t t = list[g * CAND_MAX + slot];
       uint32_t cw[Q::W];
       load_code<Q::W>(gcodes + (int64_t)t * CS, cw);
-      const float* tex = p.texact + ((int64_t)u * GT + g) * 256 * CS;
+      const float* tex = p.texact + ((int64_t)u * GT + g) * CS * 256;
       float e[CS];
 #pragma unroll
-      for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu) * CS + s) : 0.f;
+      for (int s = 0; s < CS; ++s) e[s] = (s < M) ? __ldcg(tex + s * 256 + ((cw[s >> 2] >> (8 * (s & 3))) & 0xffu)) : 0.f;
       float sum = 0.f;   // reference order: ((0 + T0[c0]) + T1[c1]) + ...
 #pragma unroll
       for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
@@ -791,9 +754,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
 
   // ---- histograms of every own chunk, pooled; threshold ----------------------
   for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
-  stamp(0, scta, 2);   // own chunks scored (thread 0)
+  stamp(0, scta, 7);   // own chunks scored (thread 0)
   pool_cluster<GT * HWORDS>(hist, full, R, me);
-  stamp(0, scta, 3);   // histograms pooled
+  stamp(0, scta, 8);   // histograms pooled
   if (warp < GT) {
     const int g = warp;
     const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
@@ -801,7 +764,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
   __syncthreads();
-  stamp(0, scta, 4);   // threshold known
+  stamp(0, scta, 9);   // threshold known
 
   // ---- candidates: the last scored chunk from registers, the others scored again
   emit_chunk(me + (n_mine - 1) * R);
@@ -809,7 +772,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     score_chunk(me + i * R, false, false);
     emit_chunk(me + i * R);
   }
-  stamp(0, scta, 5);   // candidates listed and rescored
+  stamp(0, scta, 10);  // candidates listed and rescored
 }
 
 template <int D, typename KVT>
@@ -968,8 +931,8 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   using AT = Attn<D, KVT>;
   constexpr int NW = AT::NW;
   extern __shared__ __align__(16) unsigned char smem[];
-  float* T = reinterpret_cast<float*>(smem);                                 // [256][CS] exact sub-table
-  uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.CS * 1024);          // [K7_CAP]
+  float* T = reinterpret_cast<float*>(smem);                                 // [M][256] exact sub-table
+  uint64_t* keys = reinterpret_cast<uint64_t*>(smem + p.M * 1024);           // [K7_CAP]
   uint32_t* hist = reinterpret_cast<uint32_t*>(keys + K7_CAP);               // [256]
   int* sel = reinterpret_cast<int*>(hist + 256);                             // [TOPK_MAX]
   float* part = reinterpret_cast<float*>(sel + TOPK_MAX);                    // [NW][D + 2]
@@ -991,7 +954,6 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   const int64_t sel_base = ((int64_t)b * Hq + hq) * sel_cap;
 
   stamp(1, blockIdx.x, 0);
-  pdl_launch_dependents();   // the next layer's k5 may start its prefetches; it waits for this grid
   for (int d = tid; d < D; d += K7_THREADS)
     s_q[d] = load_as_f32(p.q, p.q_dtype, (int64_t)b * p.q_sb + (int64_t)hq * D + d);
   if (tid == 0) s_n = 0;
@@ -1087,8 +1049,8 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
       }
       __syncthreads();
       if (s_over) {   // exact sub-table of this head, for the rescan of overflowed chunks
-        const float* tex = p.texact + ((int64_t)u * p.GT + g) * 256 * p.CS;
-        for (int i = tid; i < p.CS * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
+        const float* tex = p.texact + ((int64_t)u * p.GT + g) * p.CS * 256;
+        for (int i = tid; i < M * 64; i += K7_THREADS) cp_async16(T + i * 4, tex + i * 4);
       }
       const int n_listed = s_off[p.n_chunks];
       for (int i = tid; i < cr.sink; i += K7_THREADS) sel[i] = i;
@@ -1154,7 +1116,7 @@ __global__ void __launch_bounds__(K7_THREADS) k7_select_attend(Cdc03P p) {
   #pragma unroll
                 for (int w = 0; w < 8; ++w) cw[w] = (w < p.CS / 4) ? __ldg(row + w) : 0u;   // one row, loads in flight together
                 float sum = 0.f;
-                for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu) * p.CS + s2]);
+                for (int s2 = 0; s2 < M; ++s2) sum = fadd(sum, T[s2 * 256 + ((cw[s2 >> 2] >> (8 * (s2 & 3))) & 0xffu)]);
                 fn(sel_key(fmul(sum, scale), (uint32_t)t), n_listed + s_ooff[c] + (t - clo));
               }
             }

@@ -63,7 +63,7 @@ __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 // ---- phase stamps (profiling build only) ----------------------------------
 // Built with -DHOKV_STAMPS, the decode kernels record %globaltimer at their
 // phase boundaries (thread 0 of each CTA) into g_stamps[kernel][cta][phase]
-// (kernel 0: candidate stream, 1: attention, 2: tables);
+// (kernel 0: candidate stage, 1: attention, 2: reserved);
 // hokv_phase_stamps() copies them out.  The product build compiles no stamp.
 constexpr int STAMP_CTAS = 4096;
 constexpr int STAMP_N = 16;

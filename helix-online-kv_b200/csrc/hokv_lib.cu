@@ -97,25 +97,16 @@ static int launch_ex(K kernel, dim3 grid, dim3 block, size_t sm, cudaStream_t st
   return check_launch(what);
 }
 
-// Stage 1: K5 (tables, one CTA per unit, programmatic launch: it prefetches
-// its codebook rows into L2 while the previous kernel of the stream drains and
-// waits for it before any other access) then K6 (candidates, one thread-block
-// cluster of min(chunks, K6_CLUSTER_MAX) CTAs per unit, programmatic launch
-// once K5 has stored its image; it waits for K5 before it reads the image).
+// Stage 1: one thread-block cluster of min(chunks, K6_CLUSTER_MAX) CTAs per
+// unit builds the tables and streams the candidates (ordinary launch: it
+// reads the queries).
 template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
-  const size_t sm5 = k5_smem_bytes<CS, GT>(p.D);   // entries for the ranges, queries
-  if (int e = ensure_smem(k5_tables<CS, GT>, sm5)) return e;
-  if (int e = launch_ex(k5_tables<CS, GT>, dim3((unsigned)(p.B * p.Hkv)), dim3(K5_THREADS), sm5, st, p,
-                        "k5_tables", true))
-    return e;
   const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
   const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
   if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
-  // an ordinary launch: every cluster of the grid is placed at once on an idle
-  // GPU (a programmatic launch behind k5 left some clusters for a second wave)
   return launch_ex(k6_candidates<CS, GT>, dim3((unsigned)R, (unsigned)(p.B * p.Hkv)), dim3(K6_THREADS), sm, st, p,
                    "k6_candidates", false, R);
 }
@@ -140,7 +131,7 @@ static int qimg_bytes_for(int CS, int GT) {
 // Stage 2: K7, programmatic launch (hot-window attention overlaps K6).
 template <int D, typename KVT>
 static int launch_k7(const Cdc03P& p, cudaStream_t st) {
-  const size_t sm = (size_t)p.CS * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
+  const size_t sm = (size_t)p.M * 1024 + (size_t)K7_CAP * 8 + 1024 + (size_t)TOPK_MAX * 4 +
                     (size_t)(K7_THREADS / 32) * (D + 2) * 4 + (size_t)K7_KEYCACHE_BYTES;
   if (int e = ensure_smem(k7_select_attend<D, KVT>, sm)) return e;
   return launch_ex(k7_select_attend<D, KVT>, dim3((unsigned)(p.B * p.Hkv * p.G)), dim3(K7_THREADS), sm, st, p,
@@ -502,9 +493,9 @@ static int gt_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct Plan {
   int n_chunks, chunk, GT, qimg_bytes;
-  size_t cand_key_bytes, cand_cnt_bytes, qimg_total, texact_bytes, margin_bytes, rows_bytes;
+  size_t cand_key_bytes, cand_cnt_bytes, qimg_total, texact_bytes, margin_bytes;
   size_t total() const {
-    return cand_key_bytes + cand_cnt_bytes + qimg_total + texact_bytes + margin_bytes + rows_bytes;
+    return cand_key_bytes + cand_cnt_bytes + qimg_total + texact_bytes + margin_bytes;
   }
 };
 
@@ -560,7 +551,6 @@ static int plan_cdc03(const hokv_cdc03_args* a, Plan* pl) {
   pl->qimg_total = a256((size_t)units * pl->qimg_bytes);
   pl->texact_bytes = a256((size_t)units * pl->GT * a->code_bytes * 256 * 4);
   pl->margin_bytes = a256((size_t)units * pl->GT * 4);
-  pl->rows_bytes = a256((size_t)units * 4);
   return HOKV_OK;
 }
 
@@ -593,8 +583,6 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   p.texact = reinterpret_cast<float*>(w);
   w += pl.texact_bytes;
   p.margin = reinterpret_cast<int*>(w);
-  w += pl.margin_bytes;
-  p.img_rows = reinterpret_cast<int*>(w);
   p.qimg_bytes = pl.qimg_bytes;
   p.n_chunks = pl.n_chunks; p.chunk = pl.chunk; p.GT = pl.GT;
   return p;

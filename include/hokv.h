@@ -239,11 +239,11 @@ int hokv_cdc03_workspace_size(const hokv_cdc03_args* a, size_t* bytes);
 /* Both stages below, in order, on `stream`. */
 int hokv_cdc03_decode(const hokv_cdc03_args* a, void* stream);
 /* Stage 1 (precompute_distance_tables + gather_pq_scores + the first half of
- * the selection, product_codebook.py:172-227, compressed_attention.py:362-383),
- * two kernels: build the sub-tables and their quantised 16-bit image, then
- * stream the PQ codes scored with the image and write, per (sequence, KV head,
- * chunk, query head), the tokens that can still reach the top-k with their
- * exact scores (selection keys) into the workspace. */
+ * the selection, product_codebook.py:172-227, compressed_attention.py:362-383):
+ * build the sub-tables, stream the PQ codes scored with quantised 16-bit
+ * tables, and write, per (sequence, KV head, chunk, query head), the tokens
+ * that can still reach the top-k with their exact scores (selection keys)
+ * into the workspace. */
 int hokv_cdc03_candidates(const hokv_cdc03_args* a, void* stream);
 /* Stage 2 (compressed_attention.py:384-403): exact top-k of the candidate
  * keys with sinks, softmax attention over the selected cold tokens plus the
@@ -297,10 +297,10 @@ int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* c
  * Profiling.  No counterpart in the reference.  A library built with
  * -DHOKV_STAMPS records, in the two decode kernels, the %globaltimer value
  * (ns) at each phase boundary, thread 0 of every CTA: out[k][cta][phase] for
- * kernel k (0: candidate stream, cta = blockIdx.y * gridDim.x + blockIdx.x;
- * 1: attention stage, cta = blockIdx.x; 2: sub-tables, cta = blockIdx.x),
- * 4096 CTAs x 16 phases each, the last launch's values.  n_values must be at
- * least 3 * 4096 * 16.  The product build returns HOKV_ERR_UNSUPPORTED.
+ * kernel k (0: candidate stage, cta = blockIdx.y * gridDim.x + blockIdx.x;
+ * 1: attention stage, cta = blockIdx.x; 2: reserved), 4096 CTAs x 16 phases
+ * each, the last launch's values.  n_values must be at least 3 * 4096 * 16.
+ * The product build returns HOKV_ERR_UNSUPPORTED.
  * ---------------------------------------------------------------------- */
 int hokv_phase_stamps(uint64_t* out, size_t n_values);
 
