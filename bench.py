@@ -691,7 +691,7 @@ def run_ours(args):
                 api_step()
             out_host.copy_(out, non_blocking=True)
             if world > 1:
-                gathered_host.copy_(gather_outputs(out[Ls - 1]), non_blocking=True)
+                gathered_host.copy_(gather_outputs(out[Ls - 1], sizes=[B] * world), non_blocking=True)
 
     e2e = {}
     for name, use_graph in (("graph", True), ("eager", False)):

@@ -43,16 +43,30 @@ def max_over_ranks(value: float, device=None) -> float:
     return float(t.item())
 
 
-def gather_outputs(local: torch.Tensor) -> torch.Tensor:
-    """Concatenate every rank's per-sequence outputs along dim 0, in rank order
-    (ranks may own different numbers of sequences)."""
+def _gather_equal(local: torch.Tensor) -> torch.Tensor:
+    """All ranks' equally shaped blocks concatenated along dim 0: one collective,
+    no host synchronisation."""
+    world = dist.get_world_size()
+    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local.contiguous())
+    return out
+
+
+def gather_outputs(local: torch.Tensor, sizes=None) -> torch.Tensor:
+    """Concatenate every rank's per-sequence outputs along dim 0, in rank order.
+    Ranks may own different numbers of sequences; `sizes` (every rank's count,
+    e.g. from shard_range) saves the exchange of the counts, and equal counts
+    take a single collective."""
     if not _ready():
         return local
     world = dist.get_world_size()
-    n = torch.tensor([local.shape[0]], dtype=torch.int64, device=local.device)
-    sizes = [torch.zeros_like(n) for _ in range(world)]
-    dist.all_gather(sizes, n)
-    sizes = [int(s.item()) for s in sizes]
+    if sizes is not None and len(set(sizes)) == 1:
+        return _gather_equal(local)
+    if sizes is None:
+        n = torch.tensor([local.shape[0]], dtype=torch.int64, device=local.device)
+        got = [torch.zeros_like(n) for _ in range(world)]
+        dist.all_gather(got, n)
+        sizes = [int(x.item()) for x in got]
     mx = max(sizes)
     pad = torch.zeros((mx,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
     pad[:local.shape[0]] = local
@@ -75,6 +89,9 @@ def gather_heads(local: torch.Tensor, n_kv_heads: int, q_per_kv: int) -> torch.T
         return local
     world = dist.get_world_size()
     counts = [len(head_shard(n_kv_heads, world, r)) * q_per_kv for r in range(world)]
+    if len(set(counts)) == 1:   # equal blocks: one collective into [world, B, c, D], then heads in rank order
+        out = _gather_equal(local).view((world,) + tuple(local.shape))
+        return out.permute(1, 0, 2, 3).reshape(local.shape[0], world * local.shape[1], *local.shape[2:])
     mx = max(counts)
     pad = torch.zeros((local.shape[0], mx) + tuple(local.shape[2:]), dtype=local.dtype, device=local.device)
     pad[:, :local.shape[1]] = local

@@ -37,6 +37,8 @@ def _worker(rank, world, port, n_seq, q):
         # per-sequence "outputs": the sequence index in every element
         out = torch.tensor([[float(i)] * 3 for i in mine]).reshape(len(mine), 3)
         full = gather_outputs(out)
+        sizes = [len(shard_range(n_seq, world, r)) for r in range(world)]
+        assert gather_outputs(out, sizes=sizes).tolist() == full.tolist()
         t = max_over_ranks(1.5 + rank)
         dist.barrier()
         dist.destroy_process_group()
