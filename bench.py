@@ -472,8 +472,9 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
     a uniform-random 1024-token prompt, batch 1, then 256 greedy decode steps,
     once through the dense cache (SDPA) and once through CDC03Cache
     (exact_layers=[0], calibration 128, hot window 256, top-128 with 4 sinks,
-    PQ 8 x 8).  Device time of the prefill and of the decode loop; greedy
-    tokens shared with the dense run; cache bytes."""
+    PQ 8 x 8).  Device time of the prefill and of the decode loop; the two
+    runs' last prefill logits and first decode-step logits (same input token)
+    compared; greedy tokens shared with the dense run; cache bytes."""
     import torch
     import transformers
     from helix_online_kv.cdc03_attention import CDC03Cache
@@ -492,7 +493,7 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
                          sink_tokens=4)
     ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
 
-    def run(make_cache, attn):
+    def run(make_cache, attn, prompt_ids, n_new, first_tok=None):
         cache = make_cache()
         if attn != "cdc03":
             model.config._attn_implementation = attn
@@ -500,10 +501,12 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
         with torch.no_grad():
             a, b, c = ev(), ev(), ev()
             a.record()
-            tok = model(ids, past_key_values=cache, use_cache=True).logits[:, -1:].argmax(-1)
+            pre = model(prompt_ids, past_key_values=cache, use_cache=True).logits[:, -1:]
+            tok = pre.argmax(-1) if first_tok is None else first_tok
+            tok0 = tok
             b.record()
             first = None
-            for i in range(new):
+            for i in range(n_new):
                 logits = model(tok, past_key_values=cache, use_cache=True).logits[:, -1:]
                 if first is None:
                     first = logits.float().flatten()
@@ -511,14 +514,19 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
                 toks.append(tok)
             c.record()
             torch.cuda.synchronize()
-        return cache, torch.cat(toks, 1).flatten(), first, a.elapsed_time(b), b.elapsed_time(c)
+        return (cache, torch.cat(toks, 1).flatten(), first, a.elapsed_time(b), b.elapsed_time(c),
+                pre.float().flatten(), tok0)
 
-    dense, d_toks, d_first, d_pre, d_dec = run(transformers.DynamicCache, "sdpa")
+    make_cdc03 = lambda: CDC03Cache(kvc, n_layers=22, batch=1, kv_heads=4, head_dim=64,   # noqa: E731
+                                    capacity=prompt + new + 1, dtype=torch.float16).attach(model)
+    # warm-up of both paths (library handles, allocator, kernels), not timed
+    run(transformers.DynamicCache, "sdpa", ids[:, :512], 8)
+    run(make_cdc03, "cdc03", ids[:, :512], 8)
+    model.config._attn_implementation = "sdpa"
+    dense, d_toks, d_first, d_pre, d_dec, d_plog, d_tok0 = run(transformers.DynamicCache, "sdpa", ids, new)
     dense_bytes = sum(t.element_size() * t.nelement() for layer in dense.layers for t in (layer.keys, layer.values))
     del dense
-    cache, c_toks, c_first, c_pre, c_dec = run(
-        lambda: CDC03Cache(kvc, n_layers=22, batch=1, kv_heads=4, head_dim=64, capacity=prompt + new + 1,
-                           dtype=torch.float16).attach(model), "cdc03")
+    cache, c_toks, c_first, c_pre, c_dec, c_plog, _ = run(make_cdc03, "cdc03", ids, new, first_tok=d_tok0)
     model.config._attn_implementation = "sdpa"
     rep = cache.memory_report()
     agree = int((c_toks == d_toks).cumprod(0).sum().item())
@@ -528,11 +536,59 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
            "cdc03_cache": {"prefill_ms": c_pre, "decode_tokens_per_s": new / (c_dec / 1e3),
                            "kv_bytes": rep["total_bytes"], "calibration_complete": rep["calibration_complete"]},
            "greedy_tokens_equal_to_dense_before_first_difference": agree,
-           "first_step_logits_cosine": float(torch.nn.functional.cosine_similarity(c_first, d_first, dim=0).item()),
-           "note": "HF eager decode loop (Python and launch overhead included); CDC-03 attends the top-128 cold "
-                   "tokens plus the 256-token hot window, so greedy tokens may part from the dense run"}
+           "prefill_logits_cosine": float(torch.nn.functional.cosine_similarity(c_plog, d_plog, dim=0).item()),
+           "first_decode_step_logits_cosine": float(
+               torch.nn.functional.cosine_similarity(c_first, d_first, dim=0).item()),
+           "note": "HF eager decode loop (Python and launch overhead included), after an untimed warm-up of "
+                   "both paths; CDC-03 attends the top-128 cold tokens plus the 256-token hot window of each "
+                   "compressed layer, and random-init weights give near-uniform attention, so greedy tokens of "
+                   "the two runs part early (the kernels' parity is tested against the oracle instead)"}
     del cache, model
     torch.cuda.empty_cache()
+    return res
+
+
+def prefill_attention_sweep(reps=10):
+    """Exact causal prefill attention of one layer (hokv_prefill_attention)
+    beside torch's SDPA on the same tensors: a 1024-token TinyLlama prompt
+    (32 query / 4 KV heads, head_dim 64, f16), and 4K and 16K Llama-3-8B
+    prompts (32 / 8 heads, head_dim 128, bf16), batch 1.  Device time per call
+    (the mean of `reps` back-to-back calls after a warm-up), causal FLOPs
+    4 * Sq * (Sq + 1) / 2 * D * H_q, the result's max deviation from SDPA."""
+    import torch
+    import torch.nn.functional as F
+    from helix_online_kv.prefill import prefill_attention
+    ev = lambda: torch.cuda.Event(enable_timing=True)   # noqa: E731
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    res = {}
+    for name, Hq, Hkv, S, D, dt in (("tinyllama_1k", 32, 4, 1024, 64, torch.float16),
+                                    ("llama3_4k", 32, 8, 4096, 128, torch.bfloat16),
+                                    ("llama3_16k", 32, 8, 16384, 128, torch.bfloat16)):
+        q = torch.randn((1, S, Hq, D), generator=gen, device="cuda").to(dt).transpose(1, 2)
+        k = torch.randn((1, Hkv, S, D), generator=gen, device="cuda").to(dt)
+        v = torch.randn((1, Hkv, S, D), generator=gen, device="cuda").to(dt)
+        ours_fn = lambda: prefill_attention(q, k, v, None, True)   # noqa: E731
+        ref_fn = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)   # noqa: E731
+        out = {}
+        for tag, fn in (("hokv", ours_fn), ("sdpa", ref_fn)):
+            r = fn()
+            torch.cuda.synchronize()
+            a, b = ev(), ev()
+            a.record()
+            for _ in range(reps):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            flops = 4.0 * S * (S + 1) / 2 * D * Hq
+            out[tag] = {"us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12}
+            out[tag + "_out"] = r
+        dev = (out.pop("hokv_out").float() - out.pop("sdpa_out").transpose(1, 2).float()).abs().max().item()
+        res[name] = {"q_heads": Hq, "kv_heads": Hkv, "tokens": S, "head_dim": D, "dtype": str(dt).split(".")[-1],
+                     "hokv_prefill_attention": out["hokv"], "torch_sdpa": out["sdpa"],
+                     "max_abs_diff_vs_sdpa": dev}
+        del q, k, v
     return res
 
 
@@ -823,7 +879,8 @@ def run_ours(args):
         for name, fn in (("encoder_sweep", lambda: encoder_sweep()),
                          ("long_context", lambda: long_context(world, rank, max(3, min(args.steps, 10)))),
                          ("head_sharded_1seq", lambda: head_sharded(world, rank, max(3, min(args.steps, 10)))),
-                         ("tinyllama_generate", lambda: tinyllama_generate() if world == 1 else {"skipped": "1 GPU only"})):
+                         ("tinyllama_generate", lambda: tinyllama_generate() if world == 1 else {"skipped": "1 GPU only"}),
+                         ("prefill_attention", lambda: prefill_attention_sweep() if world == 1 else {"skipped": "1 GPU only"})):
             try:
                 extras[name] = fn()
             except Exception as e:   # noqa: BLE001 - reported in the line

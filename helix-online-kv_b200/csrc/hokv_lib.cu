@@ -9,6 +9,7 @@
 #include "codec.cuh"
 #include "dense.cuh"
 #include "assign_tc.cuh"
+#include "prefill.cuh"
 
 #include <map>
 #include <mutex>
@@ -744,5 +745,60 @@ int hokv_age_tokens(const hokv_cdc03_args* a, const int* cold_from, const int* c
 #undef HOKV_AGE
   return check_launch("k_age_tokens");
 }
+
+int hokv_prefill_attention(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                           int q_heads, int kv_heads, int q_len, int kv_len, int head_dim, int64_t q_stride_b,
+                           int64_t q_stride_h, int64_t q_stride_s, int64_t k_stride_b, int64_t k_stride_h,
+                           int64_t k_stride_s, int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+                           int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, float scale,
+                           int causal, void* stream) {
+  HOKV_REQUIRE(q && k && v && out, "prefill_attention: null pointer");
+  HOKV_REQUIRE(batch >= 1 && batch <= 65535 && q_heads >= 1 && q_heads <= 65535 && kv_heads >= 1 &&
+                   q_heads % kv_heads == 0,
+               "prefill_attention: batch=%d q_heads=%d kv_heads=%d", batch, q_heads, kv_heads);
+  HOKV_REQUIRE(q_len >= 1 && kv_len >= 1 && (!causal || kv_len >= q_len),
+               "prefill_attention: q_len=%d kv_len=%d causal=%d (a causal call needs kv_len >= q_len)", q_len,
+               kv_len, causal);
+  if (dtype != HOKV_F16 && dtype != HOKV_BF16)
+    return fail(HOKV_ERR_UNSUPPORTED, "prefill_attention: dtype %d (f16 and bf16 only)", dtype);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(HOKV_ERR_UNSUPPORTED, "prefill_attention: head_dim %d (64 and 128 only)", head_dim);
+  // 16-byte rows: every row start and every stride a multiple of 8 elements
+  const int64_t st[12] = {q_stride_b, q_stride_h, q_stride_s, k_stride_b, k_stride_h, k_stride_s,
+                          v_stride_b, v_stride_h, v_stride_s, out_stride_b, out_stride_h, out_stride_s};
+  for (int i = 0; i < 12; ++i)
+    HOKV_REQUIRE(st[i] % 8 == 0 && st[i] >= 0, "prefill_attention: stride %lld not a multiple of 8 elements",
+                 (long long)st[i]);
+  HOKV_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16),
+               "prefill_attention: pointers must be 16-byte aligned");
+  PfArgs p;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = out;
+  p.Sq = q_len;
+  p.Skv = kv_len;
+  p.Hq = q_heads;
+  p.G = q_heads / kv_heads;
+  p.qsb = q_stride_b; p.qsh = q_stride_h; p.qss = q_stride_s;
+  p.ksb = k_stride_b; p.ksh = k_stride_h; p.kss = k_stride_s;
+  p.vsb = v_stride_b; p.vsh = v_stride_h; p.vss = v_stride_s;
+  p.osb = out_stride_b; p.osh = out_stride_h; p.oss = out_stride_s;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  const dim3 grid((unsigned)cdiv(q_len, PF_ROWS), (unsigned)q_heads, (unsigned)batch);
+#define HOKV_PF(D_, T_)                                                                                  \
+  {                                                                                                    \
+    if (int e = ensure_smem(k_prefill_attn<D_, T_>, PfGeo<D_>::SMEM)) return e;                        \
+    k_prefill_attn<D_, T_><<<grid, PF_ROWS, PfGeo<D_>::SMEM, S(stream)>>>(p);                          \
+    return check_launch("k_prefill_attn");                                                            \
+  }
+  if (head_dim == 64 && dtype == HOKV_F16) HOKV_PF(64, __half)
+  if (head_dim == 64) HOKV_PF(64, __nv_bfloat16)
+  if (dtype == HOKV_F16) HOKV_PF(128, __half)
+  HOKV_PF(128, __nv_bfloat16)
+#undef HOKV_PF
+}
+
 
 }  // extern "C"

@@ -102,6 +102,8 @@ _SIGS = {
     "hokv_age_tokens": (_c_int, [ctypes.POINTER(Cdc03Args), _vp, _vp, _c_int, _vp]),
     "hokv_dense_attention": (_c_int, [_vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_f64, _c_int, _vp, _vp, _vp, _vp,
                                       _c_sz, _vp]),
+    "hokv_prefill_attention": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int]
+                               + [_c_i64] * 12 + [_c_f32, _c_int, _vp]),
     "hokv_softmax": (_c_int, [_vp, _c_int, _c_i64, _vp, _vp, _c_sz, _vp]),
     "hokv_prefilter_mask": (_c_int, [_vp, _c_int, _vp, _c_i64, _c_int, _vp, _vp]),
     "hokv_scale_f32_to_f64": (_c_int, [_vp, _c_i64, _c_f64, _vp, _vp]),

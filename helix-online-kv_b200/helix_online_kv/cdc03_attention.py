@@ -15,9 +15,11 @@ arrays, while the model attends the dense cache.  Here:
 * ``cdc03_attention_forward`` is registered with transformers as the attention
   implementation ``"cdc03"``: a decode step (one query token) of a compressed,
   calibrated layer runs the CDC-03 kernels on the store (top-k of the cold
-  range with sinks, plus the exact hot window); prefill, exact layers and
-  layers still calibrating use SDPA on the exact K/V (for compressed layers,
-  the store's views).
+  range with sinks, plus the exact hot window); prefill (several query tokens,
+  no padding mask) of every layer runs ``prefill.prefill_attention`` on the
+  exact K/V (for compressed layers, the store's views); single-token steps of
+  exact layers and of layers still calibrating, and head dims or dtypes that
+  kernel does not take, use SDPA.
 
 Usage::
 
@@ -43,6 +45,7 @@ from .cdc03 import CDC03Store
 from .compressed_cache import CompressedKVCache
 from .config import OnlineKVConfig
 from .layer_state import LayerPhase
+from .prefill import prefill_attention, supported
 
 
 class _StoreLayer(DynamicLayer):
@@ -238,6 +241,11 @@ def cdc03_attention_forward(module, query, key, value, attention_mask, dropout: 
         out = st.decode(cache.slot(layer), query[:, :, 0, :].contiguous(), scale, cache.top_k, cache.sink_tokens,
                         cache.hot_window, out_dtype=query.dtype)
         return out.unsqueeze(1), None
+    if query.shape[2] > 1 and attention_mask is None and dropout == 0.0 and supported(query, key, value):
+        # prefill, and multi-token steps of any layer: exact attention on the tensor cores
+        causal = is_causal if is_causal is not None else getattr(module, "is_causal", True)
+        if not causal or key.shape[2] >= query.shape[2]:
+            return prefill_attention(query, key, value, scaling, is_causal=bool(causal)), None
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout, scaling=scaling,
                                   is_causal=is_causal, **kwargs)
 

@@ -178,6 +178,27 @@ int hokv_dense_attention(const float* q, const float* K, const float* V, int hea
                          const uint8_t* mask, void* scores, void* out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Exact multi-token attention (prefill, and every step of the layers kept
+ * exact): out = softmax(q k^T * scale [causal]) v per query head, with
+ * q_heads / kv_heads query heads sharing a KV head.  The reference hands the
+ * exact K/V its cache returns to the model's own attention
+ * (compressed_cache.py:72-105, parent DynamicCache.update); this replaces that
+ * call.  q [batch, q_heads, q_len, head_dim], k/v [batch, kv_heads, kv_len,
+ * head_dim], out [batch, q_heads, q_len, head_dim], each through its own
+ * element strides (b, h, s; dims contiguous, strides multiples of 8
+ * elements, pointers 16-byte aligned).  Causal: query i sits at position
+ * kv_len - q_len + i and sees keys 0..that position (kv_len >= q_len).
+ * f16/bf16 (HOKV_F16/HOKV_BF16, out in the same type), head_dim 64 or 128;
+ * other cases return HOKV_ERR_UNSUPPORTED.  fp32 accumulation; the softmax
+ * weights are rounded to the input type before the second product, as
+ * FlashAttention does. */
+int hokv_prefill_attention(const void* q, const void* k, const void* v, void* out, int dtype, int batch,
+                           int q_heads, int kv_heads, int q_len, int kv_len, int head_dim, int64_t q_stride_b,
+                           int64_t q_stride_h, int64_t q_stride_s, int64_t k_stride_b, int64_t k_stride_h,
+                           int64_t k_stride_s, int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_s,
+                           int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s, float scale,
+                           int causal, void* stream);
+
 /* scipy.special.softmax over n values stored f32 (is_f64 = 0) or f64, computed
  * in f64 (compressed_attention.py:31-33). */
 int hokv_softmax(const void* in, int is_f64, int64_t n, void* out, void* workspace,
