@@ -786,11 +786,11 @@ int hokv_prefill_attention(const void* q, const void* k, const void* v, void* ou
   p.osb = out_stride_b; p.osh = out_stride_h; p.oss = out_stride_s;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
-  const dim3 grid((unsigned)cdiv(q_len, PF_ROWS), (unsigned)q_heads, (unsigned)batch);
+  const dim3 grid((unsigned)cdiv(q_len, 2 * PF_ROWS), (unsigned)q_heads, (unsigned)batch);
 #define HOKV_PF(D_, T_)                                                                                  \
   {                                                                                                    \
     if (int e = ensure_smem(k_prefill_attn<D_, T_>, PfGeo<D_>::SMEM)) return e;                        \
-    k_prefill_attn<D_, T_><<<grid, PF_ROWS, PfGeo<D_>::SMEM, S(stream)>>>(p);                          \
+    k_prefill_attn<D_, T_><<<grid, PF_THREADS, PfGeo<D_>::SMEM, S(stream)>>>(p);                       \
     return check_launch("k_prefill_attn");                                                            \
   }
   if (head_dim == 64 && dtype == HOKV_F16) HOKV_PF(64, __half)

@@ -2,60 +2,81 @@
 // the layers kept exact), FlashAttention-style on the tensor cores.
 //
 // The reference runs these through the model's own attention (its exact
-// layers and every prefill see the dense K/V, compressed_cache.py:73-105);
-// here one launch covers a layer: grid (query tiles, query heads, batch), one
-// CTA per 128 query rows of one head, looping over key/value tiles of BN
-// tokens up to the causal limit.  Per tile:
-//   S = Q K^T            tcgen05.mma kind::f16 (f16 or bf16 operands in shared
-//                        memory, fp32 accumulator: BN columns of tensor memory)
-//   P = exp2(S * scale * log2 e - m)   one thread per row (its TMEM lane),
-//                        written back as f16/bf16 in shared memory
-//   O += P V             tcgen05.mma into D more columns of tensor memory
-// with the online softmax's running maximum m raised lazily: O and the running
-// sum are rescaled only when a row's maximum grows by more than 2^8 (the
-// exponentials stay below 2^8, the normalisation by the same m at the end
-// makes the result independent of when m was raised).
+// layers and every prefill see the dense K/V, compressed_cache.py:72-105);
+// here one launch covers a layer.  Grid (query-tile pairs, query heads,
+// batch): a CTA owns 2 x 128 query rows of one head and loops over key/value
+// tiles of BN tokens up to the causal limit.  Per tile and query tile q:
+//   S_q = Q_q K^T         tcgen05.mma kind::f16 (f16 or bf16 operands in
+//                         shared memory, fp32 accumulator in tensor memory)
+//   P_q = 2^(S_q * scale * log2 e - m)   one thread per query row (its TMEM
+//                         lane), rounded to the input type into shared memory
+//   O_q += P_q V          tcgen05.mma into tensor memory
+// The two query tiles take turns on the tensor cores: while the softmax
+// warps of one tile work, the other tile's products run.  The running
+// maximum m is raised lazily: O and the running sum are rescaled only when a
+// row's maximum grows by more than 8 (log2 units), so P stays below 2^8 and
+// the final normalisation by the same m gives the exact softmax.
 //
-// Operands are K-major core matrices without swizzle (8 rows x 16 bytes,
-// 128 contiguous bytes): element (r, k) of a tile with KE 16-bit elements per
-// row lives at (r / 8) (KE / 8) 128 + (k / 8) 128 + (r % 8) 16 + (k % 8) 2
-// bytes; one K = 16 step of an MMA is two adjacent core-matrix columns.  Q and
-// K tiles are copied in that layout with cp.async; V^T (the B operand of
-// P V, K = tokens) is built from raw V rows with ldmatrix.trans.  Keys past
-// the sequence and queries past the last row are zero-filled and masked.
-// One elected thread issues the MMAs and commits them to mbarriers; every
-// wait is bounded and decided for the whole CTA at once.
+// Roles (320 threads): warps 0-3 the softmax of query tile 0 (thread = row =
+// TMEM lane), warps 4-7 that of tile 1, warp 8 loads (cp.async, completion
+// signalled on mbarriers), warp 9 lane 0 issues the MMAs and commits them to
+// mbarriers.  K and V stream through a ring of PF_STAGES tiles, so the loads
+// run up to three tiles ahead of the products.
+//
+// Shared-memory tiles are "chunk-major": element (r, k) of a tile of R rows
+// lives at (k / 8) * R * 16 + r * 16 + (k % 8) * 2 bytes, i.e. 8-element
+// (16-byte) chunks of R consecutive rows, so 8 rows x 16 bytes form one
+// 128-byte core matrix.  Read K-major (Q, K as the B of Q K^T, P): stride
+// byte offset 128 between 8-row groups, leading byte offset R * 16 between
+// K chunks.  V (rows = tokens) serves directly as the B of P V in the
+// MN-major form: leading byte offset 128 between 8-token groups, stride
+// byte offset BN * 16 between 8-dim groups.  No transposition anywhere.
+// Keys past the sequence and queries past the last row are zero-filled and
+// masked.  Every wait is bounded; a wait that gives up stops the CTA's roles
+// and sets HOKV_ERR_TIMEOUT.
 #pragma once
 #include <type_traits>
 #include "assign_tc.cuh"
 
 namespace hokv {
 
-constexpr int PF_ROWS = 128;     // query rows per CTA = TMEM lanes = threads
-constexpr int PF_TMEM_COLS = 256;
+constexpr int PF_ROWS = 128;                 // rows of a query tile = TMEM lanes
+constexpr int PF_THREADS = 320;              // 8 softmax warps, 1 load warp, 1 MMA warp
+constexpr int PF_TMEM_COLS = 512;            // S_0, S_1 (128 each), O_0, O_1 (128 each)
+constexpr int PF_STAGES = 4;                 // K/V ring depth
 
 template <int D>
 struct PfGeo {
-  static constexpr int BN = D == 64 ? 128 : 64;      // key/value tokens per tile
-  static constexpr int VR_STRIDE = D * 2 + 16;       // padded raw V row (conflict-free ldmatrix)
-  static constexpr int Q_BYTES = PF_ROWS * D * 2;
-  static constexpr int K_BYTES = BN * D * 2;
-  static constexpr int VR_BYTES = BN * VR_STRIDE;
-  static constexpr int VT_BYTES = D * BN * 2;
-  static constexpr int P_BYTES = PF_ROWS * BN * 2;
-  static constexpr int SMEM = Q_BYTES + K_BYTES + VR_BYTES + VT_BYTES + P_BYTES + 64;
-  static constexpr int O_COL = 128;                  // O accumulator columns [128, 128 + D)
+  static constexpr int BN = D == 64 ? 128 : 64;            // key/value tokens per tile
+  static constexpr int Q_BYTES = PF_ROWS * D * 2;          // one query tile
+  static constexpr int KV_BYTES = BN * D * 2;              // one K or V tile
+  static constexpr int P_BYTES = PF_ROWS * BN * 2;         // one P tile
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * PF_STAGES * KV_BYTES + 2 * P_BYTES + 128;   // 224 KB + barriers
 };
 
-__device__ __forceinline__ uint32_t cm16(int r, int k, int ke) {
-  return (uint32_t)((r >> 3) * (ke >> 3) * 128 + (k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2);
+// Byte offset of element (r, k) in a chunk-major tile of `rows` rows.
+__device__ __forceinline__ uint32_t chunk_off(int r, int k, int rows) {
+  return (uint32_t)((k >> 3) * rows * 16 + r * 16 + (k & 7) * 2);
+}
+
+// Shared-memory matrix descriptor without swizzle: leading and stride byte
+// offsets given (sm_100 version bit set, base offset 0).
+__device__ __forceinline__ uint64_t umma_desc_ls(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3ffffu) >> 4);
+  d |= (uint64_t)((lbo & 0x3ffffu) >> 4) << 16;
+  d |= (uint64_t)((sbo & 0x3ffffu) >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
 }
 
 // Instruction descriptor of kind::f16: fp32 accumulator, A and B both f16
-// (fmt 0) or both bf16 (fmt 1), K-major, M = 128, N = n.
-__device__ __forceinline__ uint32_t umma_idesc_f16(int n, int bf16) {
+// (fmt 0) or both bf16 (fmt 1), A K-major, B K-major or (b_mn) MN-major,
+// M = 128, N = n.
+__device__ __forceinline__ uint32_t umma_idesc_f16(int n, int bf16, int b_mn) {
   const uint32_t f = bf16 ? 1u : 0u;
-  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(PF_ROWS >> 4) << 24);
+  return (1u << 4) | (f << 7) | (f << 10) | ((uint32_t)(b_mn ? 1 : 0) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(PF_ROWS >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, int accumulate) {
@@ -91,8 +112,10 @@ __device__ __forceinline__ void pf_cp_async16(void* dst, const void* src, int sr
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
 }
-__device__ __forceinline__ void pf_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void pf_cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void pf_cp_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -107,6 +130,100 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 2^x (MUFU ex2, flush-to-zero); the softmax weights are rounded to 16 bits
+// afterwards, far coarser than its error.
+__device__ __forceinline__ float pf_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Largest raw score of this thread's row of S (BN TMEM columns from
+// s_addr); with MASK, columns j >= lim do not count.
+template <bool MASK, int BN>
+__device__ __forceinline__ float pf_row_max(uint32_t s_addr, int lim) {
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    tmem_ld32(s_addr + c * 32, v);
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      m0 = fmaxf(m0, MASK && c * 32 + j >= lim ? -INFINITY : v[j]);
+      m1 = fmaxf(m1, MASK && c * 32 + j + 1 >= lim ? -INFINITY : v[j + 1]);
+    }
+  }
+  return fmaxf(m0, m1);
+}
+
+// P = 2^(S * sl2 + nm) of this thread's row into the chunk-major P tile
+// (row `row` of PF_ROWS, BN columns), masked columns 0; returns the row's sum
+// of P (fp32, before rounding to T).
+template <bool MASK, int BN, typename T>
+__device__ __forceinline__ float pf_emit(uint32_t s_addr, unsigned char* sP, int row, float sl2, float nm, int lim) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    tmem_ld32(s_addr + c * 32, v);
+#pragma unroll
+    for (int j8 = 0; j8 < 4; ++j8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int j = j8 * 8 + h * 2;
+        float e0 = pf_ex2(fmaf(v[j], sl2, nm)), e1 = pf_ex2(fmaf(v[j + 1], sl2, nm));
+        if (MASK) {
+          e0 = c * 32 + j < lim ? e0 : 0.f;
+          e1 = c * 32 + j + 1 < lim ? e1 : 0.f;
+        }
+        s0 += e0;
+        s1 += e1;
+        w[h] = pack2<T>(e0, e1);
+      }
+      *reinterpret_cast<uint4*>(sP + chunk_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  return s0 + s1;
+}
+
+// Single-pass form for 64-column tiles: the row of S stays in registers
+// (va: columns 0-31, vb: 32-63) between the maximum and the exponentials.
+template <bool MASK>
+__device__ __forceinline__ float pf_max_regs(const float (&va)[32], const float (&vb)[32], int lim) {
+  float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    m0 = fmaxf(m0, MASK && j >= lim ? -INFINITY : va[j]);
+    m1 = fmaxf(m1, MASK && 32 + j >= lim ? -INFINITY : vb[j]);
+  }
+  return fmaxf(m0, m1);
+}
+
+template <bool MASK, typename T>
+__device__ __forceinline__ float pf_emit_regs(const float (&v)[32], int c, unsigned char* sP, int row, float sl2,
+                                              float nm, int lim) {
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int j = j8 * 8 + h * 2;
+      float e0 = pf_ex2(fmaf(v[j], sl2, nm)), e1 = pf_ex2(fmaf(v[j + 1], sl2, nm));
+      if (MASK) {
+        e0 = c * 32 + j < lim ? e0 : 0.f;
+        e1 = c * 32 + j + 1 < lim ? e1 : 0.f;
+      }
+      s0 += e0;
+      s1 += e1;
+      w[h] = pack2<T>(e0, e1);
+    }
+    *reinterpret_cast<uint4*>(sP + chunk_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  return s0 + s1;
+}
+
 struct PfArgs {
   const void* q;
   const void* k;
@@ -118,222 +235,266 @@ struct PfArgs {
   int causal;
 };
 
-// grid (query tiles, Hq, B), PF_ROWS threads.  Thread r owns query row r of
-// the tile (TMEM lane r).
+// Warp-uniform bounded wait (every lane of the calling warp waits on `bar`).
+__device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, unsigned parity, volatile uint32_t* abort_flag) {
+  const bool ok = !*abort_flag && mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// grid (ceil(Sq / 256), Hq, B), PF_THREADS threads.
 template <int D, typename T>
-__global__ void __launch_bounds__(PF_ROWS, 1) k_prefill_attn(const PfArgs p) {
+__global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) {
   using PG = PfGeo<D>;
   constexpr int BN = PG::BN;
-  constexpr int BF = sizeof(T) == 2 && !std::is_same<T, __half>::value ? 1 : 0;
+  constexpr int BF = std::is_same<T, __half>::value ? 0 : 1;
   extern __shared__ __align__(1024) unsigned char pf_smem[];
-  unsigned char* sQ = pf_smem;
-  unsigned char* sK = sQ + PG::Q_BYTES;
-  unsigned char* sVr = sK + PG::K_BYTES;
-  unsigned char* sVt = sVr + PG::VR_BYTES;
-  unsigned char* sP = sVt + PG::VT_BYTES;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(sP + PG::P_BYTES);
-  uint64_t* bar_o = bar_s + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_o + 1);
+  unsigned char* sQ = pf_smem;                                   // [2 tiles][Q_BYTES]
+  unsigned char* sK = sQ + 2 * PG::Q_BYTES;                      // [PF_STAGES][KV_BYTES]
+  unsigned char* sV = sK + PF_STAGES * PG::KV_BYTES;             // [PF_STAGES][KV_BYTES]
+  unsigned char* sP = sV + PF_STAGES * PG::KV_BYTES;             // [2 tiles][P_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * PG::P_BYTES);
+  uint64_t* q_full = bars;                          // loader lanes (32)
+  uint64_t* kv_full = bars + 1;                     // [PF_STAGES] loader lanes (32)
+  uint64_t* kv_empty = kv_full + PF_STAGES;         // [PF_STAGES] MMA commit
+  uint64_t* s_full = kv_empty + PF_STAGES;          // [2] MMA commit
+  uint64_t* p_full = s_full + 2;                    // [2] softmax warps (4)
+  uint64_t* o_final = p_full + 2;                   // [2] MMA commit
+  uint32_t* ctl = reinterpret_cast<uint32_t*>(o_final + 2);      // [0] tmem base, [1] abort
+  volatile uint32_t* abort_flag = &ctl[1];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_qt = (p.Sq + PF_ROWS - 1) / PF_ROWS;
-  const int qt = n_qt - 1 - (int)blockIdx.x;          // the longest (causal) tiles first
+  const int n_pairs = (p.Sq + 2 * PF_ROWS - 1) / (2 * PF_ROWS);
+  const int q0 = (n_pairs - 1 - (int)blockIdx.x) * 2 * PF_ROWS;   // the longest (causal) tiles first
   const int hq = blockIdx.y, b = blockIdx.z, hk = hq / p.G;
-  const int q0 = qt * PF_ROWS;
-  const int off = p.Skv - p.Sq;                       // absolute position of query row 0
-  const T* qg = reinterpret_cast<const T*>(p.q) + b * p.qsb + hq * p.qsh;
-  const T* kg = reinterpret_cast<const T*>(p.k) + b * p.ksb + hk * p.ksh;
-  const T* vg = reinterpret_cast<const T*>(p.v) + b * p.vsb + hk * p.vsh;
-  const int last_pos = off + min(q0 + PF_ROWS, p.Sq) - 1;
-  const int kv_end = p.causal ? min(p.Skv, last_pos + 1) : p.Skv;
-  const int n_kt = (kv_end + BN - 1) / BN;
+  const int off = p.Skv - p.Sq;                                   // absolute position of query row 0
+  int n_kt_q[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int base = q0 + q * PF_ROWS;
+    if (base >= p.Sq) {
+      n_kt_q[q] = 0;
+    } else {
+      const int last_pos = off + min(base + PF_ROWS, p.Sq) - 1;
+      const int kv_end = p.causal ? min(p.Skv, last_pos + 1) : p.Skv;
+      n_kt_q[q] = (kv_end + BN - 1) / BN;
+    }
+  }
+  const int n_kt = max(n_kt_q[0], n_kt_q[1]);
 
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+  if (warp == 9) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(ctl)),
                  "r"(PF_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
-  }
-
-  // ---- prologue: Q tile, K and V of tile 0 ----------------------------------
-  constexpr int QCH = D / 8;   // 16-byte chunks per row
-  for (int i = tid; i < PF_ROWS * QCH; i += PF_ROWS) {
-    const int r = i / QCH, c = i % QCH;
-    const bool in = q0 + r < p.Sq;
-    pf_cp_async16(sQ + cm16(r, c * 8, D), qg + (in ? (int64_t)(q0 + r) * p.qss + c * 8 : 0), in ? 16 : 0);
-  }
-  auto load_k = [&](int kt) {
-    for (int i = tid; i < BN * QCH; i += PF_ROWS) {
-      const int r = i / QCH, c = i % QCH, t = kt * BN + r;
-      const bool in = t < p.Skv;
-      pf_cp_async16(sK + cm16(r, c * 8, D), kg + (in ? (int64_t)t * p.kss + c * 8 : 0), in ? 16 : 0);
+    mbar_init(q_full, 32);
+    for (int i = 0; i < PF_STAGES; ++i) {
+      mbar_init(&kv_full[i], 32);
+      mbar_init(&kv_empty[i], 1);
     }
-  };
-  auto load_v = [&](int kt) {
-    for (int i = tid; i < BN * QCH; i += PF_ROWS) {
-      const int r = i / QCH, c = i % QCH, t = kt * BN + r;
-      const bool in = t < p.Skv;
-      pf_cp_async16(sVr + r * PG::VR_STRIDE + c * 16, vg + (in ? (int64_t)t * p.vss + c * 8 : 0), in ? 16 : 0);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_final[i], 1);
     }
-  };
-  load_k(0);
-  load_v(0);
-  pf_cp_commit();
+    ctl[1] = 0u;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-  const uint32_t idesc_s = umma_idesc_f16(BN, BF), idesc_o = umma_idesc_f16(D, BF);
-  const int pos = off + q0 + tid;                     // this row's absolute position
-  float m_run = -INFINITY, l_run = 0.f;
-  bool ok = true;   // the same on every thread: each wait's outcome is and-ed over the CTA
+  const uint32_t tmem = ctl[0];
+  auto give_up = [&]() {
+    if (atomicExch(const_cast<uint32_t*>(abort_flag), 1u) == 0u) dev_flag(HOKV_ERR_TIMEOUT);
+  };
 
-  for (int kt = 0; kt < n_kt; ++kt) {
-    // (a) K_kt and V_kt are in shared memory
-    pf_cp_wait_all();
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    // (b) S = Q K^T into columns [0, BN)
-    if (tid == 0) {
+  if (warp < 8) {
+    // ---- softmax of query tile q, one row per thread ------------------------------
+    const int q = warp >> 2, row = tid & (PF_ROWS - 1);
+    const int base = q0 + q * PF_ROWS;
+    const int pos = off + base + row;                 // this row's absolute position
+    const uint32_t lane_sel = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_sel + (uint32_t)(q * 128);
+    const uint32_t o_addr = tmem + lane_sel + (uint32_t)(256 + q * 128);
+    unsigned char* sPq = sP + q * PG::P_BYTES;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int kt = 0; kt < n_kt_q[q]; ++kt) {
+      if (!pf_wait_warp(&s_full[q], (unsigned)(kt & 1), abort_flag)) { ok = false; break; }
       tc_fence_after();
+      const int t0 = kt * BN;
+      const bool masked = t0 + BN > p.Skv || (p.causal && t0 + BN - 1 > off + base);   // warp-uniform
+      const int lim = (p.causal ? min(p.Skv, pos + 1) : p.Skv) - t0;
+      float va[32], vb[32];   // BN == 64: the row of S, read once
+      if constexpr (BN == 64) {
+        tmem_ld32(s_addr, va);
+        tmem_ld32(s_addr + 32, vb);
+      }
+      float mt;
+      if constexpr (BN == 64)
+        mt = masked ? pf_max_regs<true>(va, vb, lim) : pf_max_regs<false>(va, vb, lim);
+      else
+        mt = masked ? pf_row_max<true, BN>(s_addr, lim) : pf_row_max<false, BN>(s_addr, lim);
+      mt *= p.scale_log2;
+      const bool grow = mt > m_run + 8.f;
+      const float m_new = grow ? mt : m_run;
+      const float f = grow ? pf_ex2(m_run - m_new) : 1.f;   // 0 on the first tile
+      // O_q was last written by P V of the previous tile, which completed
+      // before S of this one (one issuing thread, in order)
+      if (kt > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(o_addr + c * 32, o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] *= f;
+          tmem_st32(o_addr + c * 32, o);
+        }
+      }
+      m_run = m_new;
+      float ls;
+      if constexpr (BN == 64) {
+        ls = masked ? pf_emit_regs<true, T>(va, 0, sPq, row, p.scale_log2, -m_run, lim) +
+                          pf_emit_regs<true, T>(vb, 1, sPq, row, p.scale_log2, -m_run, lim)
+                    : pf_emit_regs<false, T>(va, 0, sPq, row, p.scale_log2, -m_run, lim) +
+                          pf_emit_regs<false, T>(vb, 1, sPq, row, p.scale_log2, -m_run, lim);
+      } else {
+        ls = masked ? pf_emit<true, BN, T>(s_addr, sPq, row, p.scale_log2, -m_run, lim)
+                    : pf_emit<false, BN, T>(s_addr, sPq, row, p.scale_log2, -m_run, lim);
+      }
+      l_run = l_run * f + ls;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[q]);
+    }
+    if (n_kt_q[q] > 0) {
+      if (!ok || !pf_wait_warp(&o_final[q], 0u, abort_flag)) {
+        give_up();
+      } else {
+        tc_fence_after();
+        const float inv = 1.f / l_run;
+        const bool row_ok = base + row < p.Sq;
+        T* og = reinterpret_cast<T*>(p.out) + b * p.osb + hq * p.osh + (int64_t)(base + row) * p.oss;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(o_addr + c * 32, o);
+          if (row_ok) {
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8) {
+              uint4 w;
+              w.x = pack2<T>(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
+              w.y = pack2<T>(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
+              w.z = pack2<T>(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
+              w.w = pack2<T>(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(og + c * 32 + j8 * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ---- loads: both query tiles, then K and V tiles through the ring ----------
+    const T* qg = reinterpret_cast<const T*>(p.q) + b * p.qsb + hq * p.qsh;
+    const T* kg = reinterpret_cast<const T*>(p.k) + b * p.ksb + hk * p.ksh;
+    const T* vg = reinterpret_cast<const T*>(p.v) + b * p.vsb + hk * p.vsh;
+    constexpr int CH = D / 8;                          // 16-byte chunks per row
+    // lane -> (row 8 i + lane / 4, chunk 4 j + lane % 4): 64 contiguous bytes of
+    // 8 rows per instruction, 4 conflict-free shared-memory wavefronts
+    for (int i = lane; i < 2 * PF_ROWS * CH; i += 32) {
+      const int blk = i >> 5, l = i & 31;
+      const int r = (blk / (CH / 4)) * 8 + (l >> 2), c = (blk % (CH / 4)) * 4 + (l & 3);
+      const int qq = r / PF_ROWS, rr = r % PF_ROWS, gr = q0 + r;
+      const bool in = gr < p.Sq;
+      pf_cp_async16(sQ + qq * PG::Q_BYTES + chunk_off(rr, c * 8, PF_ROWS),
+                    qg + (in ? (int64_t)gr * p.qss + c * 8 : 0), in ? 16 : 0);
+    }
+    pf_cp_arrive(q_full);
+    for (int kt = 0; kt < n_kt; ++kt) {
+      const int st = kt % PF_STAGES;   // use kt / PF_STAGES of the stage waits for the previous use's release
+      if (kt >= PF_STAGES && !pf_wait_warp(&kv_empty[st], (unsigned)((kt / PF_STAGES + 1) & 1), abort_flag)) {
+        give_up();
+        break;
+      }
+      unsigned char* dk = sK + st * PG::KV_BYTES;
+      unsigned char* dv = sV + st * PG::KV_BYTES;
+      for (int i = lane; i < BN * CH; i += 32) {
+        const int blk = i >> 5, l = i & 31;
+        const int r = (blk / (CH / 4)) * 8 + (l >> 2), c = (blk % (CH / 4)) * 4 + (l & 3);
+        const int t = kt * BN + r;
+        const bool in = t < p.Skv;
+        pf_cp_async16(dk + chunk_off(r, c * 8, BN), kg + (in ? (int64_t)t * p.kss + c * 8 : 0), in ? 16 : 0);
+        pf_cp_async16(dv + chunk_off(r, c * 8, BN), vg + (in ? (int64_t)t * p.vss + c * 8 : 0), in ? 16 : 0);
+      }
+      pf_cp_arrive(&kv_full[st]);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (lane == 0) {
+    // ---- MMA issue -----------------------------------------------------------------
+    const uint32_t idesc_s = umma_idesc_f16(BN, BF, 0), idesc_o = umma_idesc_f16(D, BF, 1);
+    const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+    bool ok = !*abort_flag && mbar_wait(q_full, 0u);
+    auto issue_s = [&](int q, int kt) {   // S_q = Q_q K(kt)^T, committed to s_full[q]
+      const uint32_t a = aQ + q * PG::Q_BYTES, bk = aK + (kt % PF_STAGES) * PG::KV_BYTES;
 #pragma unroll
       for (int kc = 0; kc < D / 16; ++kc)
-        umma_f16(tmem, umma_desc(smem_u32(sQ) + kc * 256, (D / 8) * 128), umma_desc(smem_u32(sK) + kc * 256, (D / 8) * 128),
-                 idesc_s, kc > 0);
-      umma_commit(bar_s);
-    }
-    // (c) the previous P V has finished reading V^T and P
-    if (kt > 0) {
-      ok = __syncthreads_and(mbar_wait(bar_o, (unsigned)((kt - 1) & 1)));
-      if (!ok) break;
+        umma_f16(tmem + (uint32_t)(q * 128), umma_desc_ls(a + kc * 2 * PF_ROWS * 16, PF_ROWS * 16, 128),
+                 umma_desc_ls(bk + kc * 2 * BN * 16, BN * 16, 128), idesc_s, kc > 0);
+      umma_commit(&s_full[q]);
+    };
+    auto wait_kv = [&](int kt) {
+      if (ok && !(*abort_flag) && mbar_wait(&kv_full[kt % PF_STAGES], (unsigned)((kt / PF_STAGES) & 1))) {
+        fence_async_smem();
+        tc_fence_after();
+      } else {
+        ok = false;
+      }
+    };
+    if (ok) {
+      fence_async_smem();
       tc_fence_after();
     }
-    // (d) V^T of this tile from the raw rows: each ldmatrix.x4.trans moves four
-    //     8 x 8 blocks (8 tokens x 32 dims)
-    for (int blk = warp; blk < (BN / 8) * (D / 32); blk += PF_ROWS / 32) {
-      const int ck = blk / (D / 32), d0 = (blk % (D / 32)) * 32;
-      const unsigned char* src = sVr + (ck * 8 + (lane & 7)) * PG::VR_STRIDE + (d0 + 8 * (lane >> 3)) * 2;
-      uint32_t r0, r1, r2, r3;
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                   : "r"(smem_u32(src)));
-      const int dr = lane >> 2, kk = ck * 8 + 2 * (lane & 3);
-      *reinterpret_cast<uint32_t*>(sVt + cm16(d0 + dr, kk, BN)) = r0;
-      *reinterpret_cast<uint32_t*>(sVt + cm16(d0 + 8 + dr, kk, BN)) = r1;
-      *reinterpret_cast<uint32_t*>(sVt + cm16(d0 + 16 + dr, kk, BN)) = r2;
-      *reinterpret_cast<uint32_t*>(sVt + cm16(d0 + 24 + dr, kk, BN)) = r3;
-    }
-    __syncthreads();
-    if (kt + 1 < n_kt) load_v(kt + 1);                // raw V rows are free again
-    // (e) S is ready; K may be overwritten
-    ok = __syncthreads_and(mbar_wait(bar_s, (unsigned)(kt & 1)));
-    if (!ok) break;
-    tc_fence_after();
-    if (kt + 1 < n_kt) load_k(kt + 1);
-    pf_cp_commit();
-    // (f) softmax of this row: maximum, lazy rescale, P
-    const int t0 = kt * BN;
-    const bool masked = t0 + BN > p.Skv || (p.causal && t0 + BN - 1 > off + q0);
-    float mt = -INFINITY;
+    if (ok && n_kt > 0) {
+      wait_kv(0);
+      if (ok) {
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_ld32(lane_base + c * 32, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = t0 + c * 32 + j;
-        const bool live = !masked || (t < p.Skv && (!p.causal || t <= pos));
-        mt = fmaxf(mt, live ? v[j] * p.scale_log2 : -INFINITY);
+        for (int q = 0; q < 2; ++q)
+          if (n_kt_q[q] > 0) issue_s(q, 0);
       }
     }
-    const bool grow = mt > m_run + 8.f;
-    const float m_new = grow ? mt : m_run;
-    const float f = grow ? exp2f(m_run - m_new) : 1.f;   // 0 on the first tile
-    if (kt > 0 && __any_sync(0xffffffffu, grow)) {
+    for (int kt = 0; ok && kt < n_kt; ++kt) {
+      bool next_ready = false;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld32(lane_base + PG::O_COL + c * 32, o);
+      for (int q = 0; q < 2; ++q) {
+        if (kt < n_kt_q[q]) {
+          // P_q(kt) written, S_q(kt) read: O_q += P_q V(kt)
+          if (*abort_flag || !mbar_wait(&p_full[q], (unsigned)(kt & 1))) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = aP + q * PG::P_BYTES, bv = aV + (kt % PF_STAGES) * PG::KV_BYTES;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] *= f;
-        tmem_st32(lane_base + PG::O_COL + c * 32, o);
-      }
-    }
-    l_run *= f;
-    m_run = m_new;
-    float ls = 0.f;
-#pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      float v[32];
-      tmem_ld32(lane_base + c * 32, v);
-#pragma unroll
-      for (int j8 = 0; j8 < 4; ++j8) {
-        uint32_t w[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float e[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int j = j8 * 8 + h * 2 + u;
-            const int t = t0 + c * 32 + j;
-            const bool live = !masked || (t < p.Skv && (!p.causal || t <= pos));
-            e[u] = live ? exp2f(v[j] * p.scale_log2 - m_run) : 0.f;
-            ls += e[u];
+          for (int kc = 0; kc < BN / 16; ++kc)
+            umma_f16(tmem + (uint32_t)(256 + q * 128), umma_desc_ls(a + kc * 2 * PF_ROWS * 16, PF_ROWS * 16, 128),
+                     umma_desc_ls(bv + kc * 2 * 128, 128, BN * 16), idesc_o, kt > 0 || kc > 0);
+          if (kt == n_kt_q[q] - 1) umma_commit(&o_final[q]);
+        }
+        if (kt + 1 < n_kt_q[q]) {
+          if (!next_ready) {
+            wait_kv(kt + 1);
+            if (!ok) break;
+            next_ready = true;
           }
-          w[h] = pack2<T>(e[0], e[1]);
-        }
-        *reinterpret_cast<uint4*>(sP + cm16(tid, c * 32 + j8 * 8, BN)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-    l_run += ls;
-    // (g) O += P V^T
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kc = 0; kc < BN / 16; ++kc)
-        umma_f16(tmem + PG::O_COL, umma_desc(smem_u32(sP) + kc * 256, (BN / 8) * 128),
-                 umma_desc(smem_u32(sVt) + kc * 256, (BN / 8) * 128), idesc_o, kt > 0 || kc > 0);
-      umma_commit(bar_o);
-    }
-  }
-  pf_cp_wait_all();
-  // ---- epilogue: O / l ---------------------------------------------------------
-  if (ok && n_kt > 0) ok = __syncthreads_and(mbar_wait(bar_o, (unsigned)((n_kt - 1) & 1)));
-  if (!ok) {
-    if (tid == 0) dev_flag(HOKV_ERR_TIMEOUT);
-  } else if (n_kt > 0) {
-    tc_fence_after();
-    const float inv = 1.f / l_run;
-    const bool row_ok = q0 + tid < p.Sq;
-    T* og = reinterpret_cast<T*>(p.out) + b * p.osb + hq * p.osh + (int64_t)(q0 + tid) * p.oss;
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float o[32];
-      tmem_ld32(lane_base + PG::O_COL + c * 32, o);
-      if (row_ok) {
-#pragma unroll
-        for (int j8 = 0; j8 < 4; ++j8) {
-          uint4 w;
-          w.x = pack2<T>(o[j8 * 8 + 0] * inv, o[j8 * 8 + 1] * inv);
-          w.y = pack2<T>(o[j8 * 8 + 2] * inv, o[j8 * 8 + 3] * inv);
-          w.z = pack2<T>(o[j8 * 8 + 4] * inv, o[j8 * 8 + 5] * inv);
-          w.w = pack2<T>(o[j8 * 8 + 6] * inv, o[j8 * 8 + 7] * inv);
-          *reinterpret_cast<uint4*>(og + c * 32 + j8 * 8) = w;
+          issue_s(q, kt + 1);
         }
       }
+      if (ok) umma_commit(&kv_empty[kt % PF_STAGES]);   // the stage is free once these products finish
     }
+    if (!ok) give_up();
   }
+  // every role is done: the last products were awaited by the softmax warps
+  // (o_final), or the CTA gave up
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS));
   }
