@@ -1044,7 +1044,12 @@ def main():
                          "whose JSON line is then not the workload's")
     ap.add_argument("--phase-stamps", action="store_true",
                     help="run one step with the profiling build (libhokv_stamps.so) and print per-phase times")
+    ap.add_argument("--prefill-sweep", action="store_true",
+                    help="only the prefill-attention sweep (hokv_prefill_attention beside SDPA), one JSON line")
     args = ap.parse_args()
+    if args.prefill_sweep:
+        print(json.dumps({"prefill_attention": prefill_attention_sweep()}))
+        return 0
     if args.phase_stamps:
         os.environ["HOKV_LIB_VARIANT"] = "stamps"   # read when the package loads the library
         return run_phase_stamps(args)

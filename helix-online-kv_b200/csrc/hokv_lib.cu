@@ -340,6 +340,71 @@ static int launch_assign_tc_sd(const void* x, int x_dtype, int64_t n, int64_t xr
   }
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// link-time libcuda dependency).
+typedef CUresult (*PfEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PfEncodeFn pf_encoder() {
+  static std::once_flag once;
+  static PfEncodeFn fn = nullptr;
+  std::call_once(once, []() {
+    cudaDriverEntryPointQueryResult qr;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfEncodeFn>(f);
+  });
+  return fn;
+}
+
+// A [batch, heads, tokens, dim] tensor with element strides (sb, sh, ss) as a
+// 4-D tensor map for 128-byte-swizzled boxes of 64 dims x `box_rows` tokens:
+// dim 0 = the head dim, dims 1-3 = tokens, heads, batch sorted by stride (a
+// dim of extent 1 takes the stride its place needs); *slot_* return each
+// dim's position.  HOKV_ERR_UNSUPPORTED when the strides do not nest.
+static int pf_tensor_map(CUtensorMap* m, const void* base, int dtype, int dim, int64_t tokens, int64_t ss,
+                         int64_t heads, int64_t sh, int64_t batch, int64_t sb, int box_rows, int* slot_t,
+                         int* slot_h, int* slot_b) {
+  PfEncodeFn enc = pf_encoder();
+  if (!enc) return fail(HOKV_ERR_CUDA, "prefill_attention: cuTensorMapEncodeTiled unavailable");
+  int64_t ext[3] = {tokens, heads, batch}, str[3] = {ss, sh, sb};
+  int order[3] = {0, 1, 2};
+  for (int i = 0; i < 3; ++i)   // ascending stride; extent-1 dims last
+    for (int j = i + 1; j < 3; ++j) {
+      const bool sw = (ext[order[j]] > 1 && ext[order[i]] == 1) ||
+                      ((ext[order[j]] > 1) == (ext[order[i]] > 1) && str[order[j]] < str[order[i]]);
+      if (sw) std::swap(order[i], order[j]);
+    }
+  cuuint64_t gdim[4] = {(cuuint64_t)dim, 0, 0, 0};
+  cuuint64_t gstr[3];
+  int64_t need = (int64_t)dim;   // elements the next stride must cover
+  for (int i = 0; i < 3; ++i) {
+    const int d = order[i];
+    gdim[i + 1] = (cuuint64_t)ext[d];
+    int64_t s = str[d];
+    if (ext[d] == 1) s = need;
+    if (s < need)
+      return fail(HOKV_ERR_UNSUPPORTED, "prefill_attention: strides (%lld, %lld, %lld) do not nest",
+                  (long long)ss, (long long)sh, (long long)sb);
+    gstr[i] = (cuuint64_t)s * 2;
+    need = s * ext[d];
+    if (d == 0) *slot_t = i + 1;
+    if (d == 1) *slot_h = i + 1;
+    if (d == 2) *slot_b = i + 1;
+  }
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  cuuint32_t bx[4] = {64, 1, 1, 1};   // 64 dims x box_rows tokens x 1 head x 1 sequence
+  bx[*slot_t] = (cuuint32_t)box_rows;
+  const CUresult r = enc(m, dtype == HOKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         4, const_cast<void*>(base), gdim, gstr, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HOKV_ERR_UNSUPPORTED, "prefill_attention: tensor map encode failed (%d)", (int)r);
+  return HOKV_OK;
+}
+
 static int launch_assign_tc(const void* x, int x_dtype, int64_t n, int64_t xrs, int64_t xss, int M, int sd,
                             const float* cents, int slots, int64_t css, const int* k, int64_t kss, uint8_t* out,
                             int64_t ors, int64_t oss, int n_sets, cudaStream_t st) {
@@ -771,18 +836,26 @@ int hokv_prefill_attention(const void* q, const void* k, const void* v, void* ou
                  (long long)st[i]);
   HOKV_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(out, 16),
                "prefill_attention: pointers must be 16-byte aligned");
+  HOKV_REQUIRE(k_stride_b == v_stride_b && k_stride_h == v_stride_h && k_stride_s == v_stride_s,
+               "prefill_attention: k and v must share their strides");
+  PfMaps maps;
   PfArgs p;
-  p.q = q;
-  p.k = k;
-  p.v = v;
+  if (int e = pf_tensor_map(&maps.q, q, dtype, head_dim, q_len, q_stride_s, q_heads, q_stride_h, batch, q_stride_b,
+                            PF_ROWS, &p.q_slot_t, &p.q_slot_h, &p.q_slot_b))
+    return e;
+  const int bn = head_dim == 64 ? PfGeo<64>::BN : PfGeo<128>::BN;
+  if (int e = pf_tensor_map(&maps.k, k, dtype, head_dim, kv_len, k_stride_s, kv_heads, k_stride_h, batch, k_stride_b,
+                            bn, &p.kv_slot_t, &p.kv_slot_h, &p.kv_slot_b))
+    return e;
+  int ts, hs, bs;
+  if (int e = pf_tensor_map(&maps.v, v, dtype, head_dim, kv_len, v_stride_s, kv_heads, v_stride_h, batch, v_stride_b,
+                            bn, &ts, &hs, &bs))
+    return e;
   p.out = out;
   p.Sq = q_len;
   p.Skv = kv_len;
   p.Hq = q_heads;
   p.G = q_heads / kv_heads;
-  p.qsb = q_stride_b; p.qsh = q_stride_h; p.qss = q_stride_s;
-  p.ksb = k_stride_b; p.ksh = k_stride_h; p.kss = k_stride_s;
-  p.vsb = v_stride_b; p.vsh = v_stride_h; p.vss = v_stride_s;
   p.osb = out_stride_b; p.osh = out_stride_h; p.oss = out_stride_s;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
@@ -790,7 +863,7 @@ int hokv_prefill_attention(const void* q, const void* k, const void* v, void* ou
 #define HOKV_PF(D_, T_)                                                                                  \
   {                                                                                                    \
     if (int e = ensure_smem(k_prefill_attn<D_, T_>, PfGeo<D_>::SMEM)) return e;                        \
-    k_prefill_attn<D_, T_><<<grid, PF_THREADS, PfGeo<D_>::SMEM, S(stream)>>>(p);                       \
+    k_prefill_attn<D_, T_><<<grid, PF_THREADS, PfGeo<D_>::SMEM, S(stream)>>>(maps, p);                 \
     return check_launch("k_prefill_attn");                                                            \
   }
   if (head_dim == 64 && dtype == HOKV_F16) HOKV_PF(64, __half)

@@ -18,23 +18,25 @@
 // the final normalisation by the same m gives the exact softmax.
 //
 // Roles (320 threads): warps 0-3 the softmax of query tile 0 (thread = row =
-// TMEM lane), warps 4-7 that of tile 1, warp 8 loads (cp.async, completion
-// signalled on mbarriers), warp 9 lane 0 issues the MMAs and commits them to
-// mbarriers.  K and V stream through a ring of PF_STAGES tiles, so the loads
-// run up to three tiles ahead of the products.
+// TMEM lane), warps 4-7 that of tile 1, warp 8 lane 0 loads the tiles with
+// TMA (cp.async.bulk.tensor, completion counted in bytes on mbarriers), warp 9
+// lane 0 issues the MMAs and commits them to mbarriers.  K and V stream
+// through a ring of PF_STAGES tiles, so the loads run up to three tiles ahead
+// of the products.
 //
-// Shared-memory tiles are "chunk-major": element (r, k) of a tile of R rows
-// lives at (k / 8) * R * 16 + r * 16 + (k % 8) * 2 bytes, i.e. 8-element
-// (16-byte) chunks of R consecutive rows, so 8 rows x 16 bytes form one
-// 128-byte core matrix.  Read K-major (Q, K as the B of Q K^T, P): stride
-// byte offset 128 between 8-row groups, leading byte offset R * 16 between
-// K chunks.  V (rows = tokens) serves directly as the B of P V in the
-// MN-major form: leading byte offset 128 between 8-token groups, stride
-// byte offset BN * 16 between 8-dim groups.  No transposition anywhere.
-// Keys past the sequence and queries past the last row are zero-filled and
-// masked.  Every wait is bounded; a wait that gives up stops the CTA's roles
+// Shared-memory tiles use the 128-byte swizzle of TMA and the tensor cores:
+// a tile of R rows x C 16-bit columns is C / 64 column blocks of R rows x
+// 128 bytes (64 elements), 16-byte chunk j of row r stored at chunk j ^ (r %
+// 8), 8-row groups 1024 bytes apart.  TMA writes Q, K and V tiles in that
+// layout from the (b, h, s) strided tensors; the softmax threads write P in
+// it.  Q, K and P are read K-major (an MMA K step of 16 columns is 32 bytes
+// inside a column block); V (rows = tokens) is read in place as the MN-major B
+// of P V: 64-dim column blocks and 8-token groups.  No transposition anywhere.
+// Keys past the sequence and queries past the last row are zero-filled by TMA
+// and masked.  Every wait is bounded; a wait that gives up stops the CTA's roles
 // and sets HOKV_ERR_TIMEOUT.
 #pragma once
+#include <cuda.h>
 #include <type_traits>
 #include "assign_tc.cuh"
 
@@ -54,19 +56,22 @@ struct PfGeo {
   static constexpr int SMEM = 2 * Q_BYTES + 2 * PF_STAGES * KV_BYTES + 2 * P_BYTES + 128;   // 224 KB + barriers
 };
 
-// Byte offset of element (r, k) in a chunk-major tile of `rows` rows.
-__device__ __forceinline__ uint32_t chunk_off(int r, int k, int rows) {
-  return (uint32_t)((k >> 3) * rows * 16 + r * 16 + (k & 7) * 2);
+// Byte offset of element (r, k) (k a multiple of 8: the start of a 16-byte
+// chunk) in a 128-byte-swizzled tile of `rows` rows.
+__device__ __forceinline__ uint32_t sw128_off(int r, int k, int rows) {
+  return (uint32_t)((k >> 6) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4));
 }
 
-// Shared-memory matrix descriptor without swizzle: leading and stride byte
-// offsets given (sm_100 version bit set, base offset 0).
-__device__ __forceinline__ uint64_t umma_desc_ls(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor with the 128-byte swizzle: leading and
+// stride byte offsets given (sm_100 version bit, base offset 0: every tile
+// starts on a 1024-byte boundary).
+__device__ __forceinline__ uint64_t umma_desc_sw(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3ffffu) >> 4);
   d |= (uint64_t)((lbo & 0x3ffffu) >> 4) << 16;
   d |= (uint64_t)((sbo & 0x3ffffu) >> 4) << 32;
   d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;   // 128-byte swizzle
   return d;
 }
 
@@ -107,14 +112,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// 16-byte global -> shared copy; src_bytes = 0 fills zeros (src not read).
-__device__ __forceinline__ void pf_cp_async16(void* dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-               : "memory");
+// TMA tile load of a 4-D tensor map (no multicast) into this CTA's shared
+// memory, completion counted in bytes on `bar`.
+__device__ __forceinline__ void pf_tma4(void* dst, const void* map, int c0, int c1, int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
 }
-// Arrive on `bar` once every cp.async this thread issued so far has landed.
-__device__ __forceinline__ void pf_cp_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void pf_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
 template <typename T>
@@ -181,7 +188,7 @@ __device__ __forceinline__ float pf_emit(uint32_t s_addr, unsigned char* sP, int
         s1 += e1;
         w[h] = pack2<T>(e0, e1);
       }
-      *reinterpret_cast<uint4*>(sP + chunk_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
   return s0 + s1;
@@ -219,21 +226,33 @@ __device__ __forceinline__ float pf_emit_regs(const float (&v)[32], int c, unsig
       s1 += e1;
       w[h] = pack2<T>(e0, e1);
     }
-    *reinterpret_cast<uint4*>(sP + chunk_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
   return s0 + s1;
 }
 
+// Tensor maps of q, k and v as 4-D (head dim, then the token, head and
+// batch dims in ascending stride order); slot_* give each dim's coordinate
+// position (1-3) in that map.
+struct alignas(64) PfMaps {
+  CUtensorMap q, k, v;
+};
+
 struct PfArgs {
-  const void* q;
-  const void* k;
-  const void* v;
   void* out;
   int Sq, Skv, Hq, G;
-  int64_t qsb, qsh, qss, ksb, ksh, kss, vsb, vsh, vss, osb, osh, oss;   // element strides
-  float scale_log2;   // softmax scale * log2(e)
+  int64_t osb, osh, oss;   // output element strides
+  int q_slot_t, q_slot_h, q_slot_b, kv_slot_t, kv_slot_h, kv_slot_b;
+  float scale_log2;        // softmax scale * log2(e)
   int causal;
 };
+
+__device__ __forceinline__ void pf_coords(int slot_t, int slot_h, int slot_b, int t, int h, int b, int (&c)[4]) {
+  c[0] = 0;
+  c[slot_t] = t;
+  c[slot_h] = h;
+  c[slot_b] = b;
+}
 
 // Warp-uniform bounded wait (every lane of the calling warp waits on `bar`).
 __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, unsigned parity, volatile uint32_t* abort_flag) {
@@ -243,7 +262,7 @@ __device__ __forceinline__ bool pf_wait_warp(uint64_t* bar, unsigned parity, vol
 
 // grid (ceil(Sq / 256), Hq, B), PF_THREADS threads.
 template <int D, typename T>
-__global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) {
+__global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const __grid_constant__ PfMaps maps, const PfArgs p) {
   using PG = PfGeo<D>;
   constexpr int BN = PG::BN;
   constexpr int BF = std::is_same<T, __half>::value ? 0 : 1;
@@ -253,8 +272,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) 
   unsigned char* sV = sK + PF_STAGES * PG::KV_BYTES;             // [PF_STAGES][KV_BYTES]
   unsigned char* sP = sV + PF_STAGES * PG::KV_BYTES;             // [2 tiles][P_BYTES]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * PG::P_BYTES);
-  uint64_t* q_full = bars;                          // loader lanes (32)
-  uint64_t* kv_full = bars + 1;                     // [PF_STAGES] loader lanes (32)
+  uint64_t* q_full = bars;                          // TMA bytes
+  uint64_t* kv_full = bars + 1;                     // [PF_STAGES] TMA bytes
   uint64_t* kv_empty = kv_full + PF_STAGES;         // [PF_STAGES] MMA commit
   uint64_t* s_full = kv_empty + PF_STAGES;          // [2] MMA commit
   uint64_t* p_full = s_full + 2;                    // [2] softmax warps (4)
@@ -287,9 +306,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) 
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(q_full, 32);
+    mbar_init(q_full, 1);
     for (int i = 0; i < PF_STAGES; ++i) {
-      mbar_init(&kv_full[i], 32);
+      mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -394,41 +413,33 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) 
       }
     }
   } else if (warp == 8) {
-    // ---- loads: both query tiles, then K and V tiles through the ring ----------
-    const T* qg = reinterpret_cast<const T*>(p.q) + b * p.qsb + hq * p.qsh;
-    const T* kg = reinterpret_cast<const T*>(p.k) + b * p.ksb + hk * p.ksh;
-    const T* vg = reinterpret_cast<const T*>(p.v) + b * p.vsb + hk * p.vsh;
-    constexpr int CH = D / 8;                          // 16-byte chunks per row
-    // lane -> (row 8 i + lane / 4, chunk 4 j + lane % 4): 64 contiguous bytes of
-    // 8 rows per instruction, 4 conflict-free shared-memory wavefronts
-    for (int i = lane; i < 2 * PF_ROWS * CH; i += 32) {
-      const int blk = i >> 5, l = i & 31;
-      const int r = (blk / (CH / 4)) * 8 + (l >> 2), c = (blk % (CH / 4)) * 4 + (l & 3);
-      const int qq = r / PF_ROWS, rr = r % PF_ROWS, gr = q0 + r;
-      const bool in = gr < p.Sq;
-      pf_cp_async16(sQ + qq * PG::Q_BYTES + chunk_off(rr, c * 8, PF_ROWS),
-                    qg + (in ? (int64_t)gr * p.qss + c * 8 : 0), in ? 16 : 0);
-    }
-    pf_cp_arrive(q_full);
-    for (int kt = 0; kt < n_kt; ++kt) {
-      const int st = kt % PF_STAGES;   // use kt / PF_STAGES of the stage waits for the previous use's release
-      if (kt >= PF_STAGES && !pf_wait_warp(&kv_empty[st], (unsigned)((kt / PF_STAGES + 1) & 1), abort_flag)) {
-        give_up();
-        break;
+    // ---- loads (lane 0): both query tiles, then K and V tiles through the ring ----
+    if (lane == 0) {
+      int c[4];
+      pf_expect_tx(q_full, 2 * PG::Q_BYTES);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        pf_coords(p.q_slot_t, p.q_slot_h, p.q_slot_b, q0 + q * PF_ROWS, hq, b, c);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a)
+          pf_tma4(sQ + q * PG::Q_BYTES + a * PF_ROWS * 128, &maps.q, a * 64, c[1], c[2], c[3], q_full);
       }
-      unsigned char* dk = sK + st * PG::KV_BYTES;
-      unsigned char* dv = sV + st * PG::KV_BYTES;
-      for (int i = lane; i < BN * CH; i += 32) {
-        const int blk = i >> 5, l = i & 31;
-        const int r = (blk / (CH / 4)) * 8 + (l >> 2), c = (blk % (CH / 4)) * 4 + (l & 3);
-        const int t = kt * BN + r;
-        const bool in = t < p.Skv;
-        pf_cp_async16(dk + chunk_off(r, c * 8, BN), kg + (in ? (int64_t)t * p.kss + c * 8 : 0), in ? 16 : 0);
-        pf_cp_async16(dv + chunk_off(r, c * 8, BN), vg + (in ? (int64_t)t * p.vss + c * 8 : 0), in ? 16 : 0);
+      for (int kt = 0; kt < n_kt; ++kt) {
+        const int st = kt % PF_STAGES;   // use kt / PF_STAGES of the stage waits for the previous use's release
+        if (kt >= PF_STAGES &&
+            (*abort_flag || !mbar_wait(&kv_empty[st], (unsigned)((kt / PF_STAGES + 1) & 1)))) {
+          give_up();
+          break;
+        }
+        pf_coords(p.kv_slot_t, p.kv_slot_h, p.kv_slot_b, kt * BN, hk, b, c);
+        pf_expect_tx(&kv_full[st], 2 * PG::KV_BYTES);
+#pragma unroll
+        for (int a = 0; a < D / 64; ++a) {
+          pf_tma4(sK + st * PG::KV_BYTES + a * BN * 128, &maps.k, a * 64, c[1], c[2], c[3], &kv_full[st]);
+          pf_tma4(sV + st * PG::KV_BYTES + a * BN * 128, &maps.v, a * 64, c[1], c[2], c[3], &kv_full[st]);
+        }
       }
-      pf_cp_arrive(&kv_full[st]);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (lane == 0) {
     // ---- MMA issue -----------------------------------------------------------------
     const uint32_t idesc_s = umma_idesc_f16(BN, BF, 0), idesc_o = umma_idesc_f16(D, BF, 1);
@@ -437,23 +448,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) 
     auto issue_s = [&](int q, int kt) {   // S_q = Q_q K(kt)^T, committed to s_full[q]
       const uint32_t a = aQ + q * PG::Q_BYTES, bk = aK + (kt % PF_STAGES) * PG::KV_BYTES;
 #pragma unroll
-      for (int kc = 0; kc < D / 16; ++kc)
-        umma_f16(tmem + (uint32_t)(q * 128), umma_desc_ls(a + kc * 2 * PF_ROWS * 16, PF_ROWS * 16, 128),
-                 umma_desc_ls(bk + kc * 2 * BN * 16, BN * 16, 128), idesc_s, kc > 0);
+      for (int kc = 0; kc < D / 16; ++kc)   // K step kc: column block kc / 4, 32 bytes per step inside it
+        umma_f16(tmem + (uint32_t)(q * 128), umma_desc_sw(a + (kc >> 2) * PF_ROWS * 128 + (kc & 3) * 32, 16, 1024),
+                 umma_desc_sw(bk + (kc >> 2) * BN * 128 + (kc & 3) * 32, 16, 1024), idesc_s, kc > 0);
       umma_commit(&s_full[q]);
     };
     auto wait_kv = [&](int kt) {
       if (ok && !(*abort_flag) && mbar_wait(&kv_full[kt % PF_STAGES], (unsigned)((kt / PF_STAGES) & 1))) {
-        fence_async_smem();
         tc_fence_after();
       } else {
         ok = false;
       }
     };
-    if (ok) {
-      fence_async_smem();
-      tc_fence_after();
-    }
+    if (ok) tc_fence_after();
     if (ok && n_kt > 0) {
       wait_kv(0);
       if (ok) {
@@ -473,8 +480,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const PfArgs p) 
           const uint32_t a = aP + q * PG::P_BYTES, bv = aV + (kt % PF_STAGES) * PG::KV_BYTES;
 #pragma unroll
           for (int kc = 0; kc < BN / 16; ++kc)
-            umma_f16(tmem + (uint32_t)(256 + q * 128), umma_desc_ls(a + kc * 2 * PF_ROWS * 16, PF_ROWS * 16, 128),
-                     umma_desc_ls(bv + kc * 2 * 128, 128, BN * 16), idesc_o, kt > 0 || kc > 0);
+            umma_f16(tmem + (uint32_t)(256 + q * 128),
+                     umma_desc_sw(a + (kc >> 2) * PF_ROWS * 128 + (kc & 3) * 32, 16, 1024),
+                     umma_desc_sw(bv + kc * 2048, BN * 128, 1024), idesc_o, kt > 0 || kc > 0);
           if (kt == n_kt_q[q] - 1) umma_commit(&o_final[q]);
         }
         if (kt + 1 < n_kt_q[q]) {

@@ -4,8 +4,10 @@ The reference's cache hands exact K/V to the model's own attention for every
 prefill and for the layers it keeps exact (compressed_cache.py:72-105).  This
 module is that attention as one CUDA launch per layer: causal (query i at
 position kv_len - q_len + i) or full, grouped-query heads read from their
-shared KV head, f16/bf16, head_dim 64 or 128, any (batch, head, token) strides
-with contiguous head dims (the CDC-03 store's views need no copy).
+shared KV head, f16/bf16, head_dim 64 or 128, (batch, head, token) strides that
+nest (any permutation of a packed layout, or a slice of one: the CDC-03 store's
+views and the transposed projections a model passes need no copy), contiguous
+head dims, key and value with the same strides.
 """
 
 from __future__ import annotations
@@ -32,6 +34,21 @@ def supported(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> bo
     for t in (query, key, value):
         if not t.is_cuda or t.stride(-1) != 1 or t.data_ptr() % 16 or any(s % 8 for s in t.stride()[:3]):
             return False
+        if not _nests(t):
+            return False
+    return key.stride() == value.stride()
+
+
+def _nests(t: torch.Tensor) -> bool:
+    """The (token, head, batch) dims, in ascending stride order, each cover the
+    dims inside them (the tensor maps the kernel loads through need this;
+    dims of extent 1 always fit)."""
+    dims = sorted(((t.stride(i), t.shape[i]) for i in (2, 1, 0) if t.shape[i] > 1))
+    need = t.shape[3]
+    for stride, extent in dims:
+        if stride < need:
+            return False
+        need = stride * extent
     return True
 
 

@@ -117,6 +117,10 @@ def test_prefill_rejects_unsupported():
     qh = q32.half()
     with pytest.raises(ValueError, match="kv_len >= q_len"):
         prefill_attention(qh, qh[:, :, :8], qh[:, :, :8])
+    # heads aliasing tokens: strides that do not nest
+    buf = torch.randn(4096, device="cuda", dtype=torch.float16)
+    alias = torch.as_strided(buf, (1, 2, 16, 64), (4096, 64, 64, 1))
+    assert not supported(alias, alias, alias)
 
 
 def test_cdc03_model_prefill_runs_the_kernel():
