@@ -137,6 +137,22 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 32 consecutive fp32 TMEM columns of this thread's lane, without waiting
+// (tcgen05.wait::ld before the values are used).
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 2^x (MUFU ex2, flush-to-zero); the softmax weights are rounded to 16 bits
 // afterwards, far coarser than its error.
 __device__ __forceinline__ float pf_ex2(float x) {
@@ -207,28 +223,34 @@ __device__ __forceinline__ float pf_max_regs(const float (&va)[32], const float 
   return fmaxf(m0, m1);
 }
 
+// Exponent arguments and the running sum use packed fp32 x 2 operations
+// (one instruction per column pair); `rowp` is the row's byte offset in its
+// P column block and x7 its swizzle key (row % 8).
 template <bool MASK, typename T>
-__device__ __forceinline__ float pf_emit_regs(const float (&v)[32], int c, unsigned char* sP, int row, float sl2,
-                                              float nm, int lim) {
-  float s0 = 0.f, s1 = 0.f;
+__device__ __forceinline__ float pf_emit_regs(const float (&v)[32], int c, unsigned char* sP, uint32_t rowp, int x7,
+                                              float sl2, float nm, int lim) {
+  float2 acc = make_float2(0.f, 0.f);
+  const float2 sl = make_float2(sl2, sl2), nn = make_float2(nm, nm);
 #pragma unroll
   for (int j8 = 0; j8 < 4; ++j8) {
     uint32_t w[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       const int j = j8 * 8 + h * 2;
-      float e0 = pf_ex2(fmaf(v[j], sl2, nm)), e1 = pf_ex2(fmaf(v[j + 1], sl2, nm));
+      const float2 a = __ffma2_rn(make_float2(v[j], v[j + 1]), sl, nn);
+      float2 e = make_float2(pf_ex2(a.x), pf_ex2(a.y));
       if (MASK) {
-        e0 = c * 32 + j < lim ? e0 : 0.f;
-        e1 = c * 32 + j + 1 < lim ? e1 : 0.f;
+        e.x = c * 32 + j < lim ? e.x : 0.f;
+        e.y = c * 32 + j + 1 < lim ? e.y : 0.f;
       }
-      s0 += e0;
-      s1 += e1;
-      w[h] = pack2<T>(e0, e1);
+      acc = __fadd2_rn(acc, e);
+      w[h] = pack2<T>(e.x, e.y);
     }
-    *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 32 + j8 * 8, PF_ROWS)) = make_uint4(w[0], w[1], w[2], w[3]);
+    const int col = c * 32 + j8 * 8;   // chunk (col % 64) / 8 of column block col / 64
+    *reinterpret_cast<uint4*>(sP + (col >> 6) * PF_ROWS * 128 + rowp + ((((col & 63) >> 3) ^ x7) << 4)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
   }
-  return s0 + s1;
+  return acc.x + acc.y;
 }
 
 // Tensor maps of q, k and v as 4-D (head dim, then the token, head and
@@ -344,9 +366,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const __grid_con
       const bool masked = t0 + BN > p.Skv || (p.causal && t0 + BN - 1 > off + base);   // warp-uniform
       const int lim = (p.causal ? min(p.Skv, pos + 1) : p.Skv) - t0;
       float va[32], vb[32];   // BN == 64: the row of S, read once
-      if constexpr (BN == 64) {
-        tmem_ld32(s_addr, va);
-        tmem_ld32(s_addr + 32, vb);
+      if constexpr (BN == 64) {   // both loads in flight, one wait
+        tmem_ld32_nw(s_addr, va);
+        tmem_ld32_nw(s_addr + 32, vb);
+        tmem_wait_ld();
       }
       float mt;
       if constexpr (BN == 64)
@@ -372,10 +395,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) k_prefill_attn(const __grid_con
       m_run = m_new;
       float ls;
       if constexpr (BN == 64) {
-        ls = masked ? pf_emit_regs<true, T>(va, 0, sPq, row, p.scale_log2, -m_run, lim) +
-                          pf_emit_regs<true, T>(vb, 1, sPq, row, p.scale_log2, -m_run, lim)
-                    : pf_emit_regs<false, T>(va, 0, sPq, row, p.scale_log2, -m_run, lim) +
-                          pf_emit_regs<false, T>(vb, 1, sPq, row, p.scale_log2, -m_run, lim);
+        const uint32_t rowp = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128);
+        ls = masked ? pf_emit_regs<true, T>(va, 0, sPq, rowp, row & 7, p.scale_log2, -m_run, lim) +
+                          pf_emit_regs<true, T>(vb, 1, sPq, rowp, row & 7, p.scale_log2, -m_run, lim)
+                    : pf_emit_regs<false, T>(va, 0, sPq, rowp, row & 7, p.scale_log2, -m_run, lim) +
+                          pf_emit_regs<false, T>(vb, 1, sPq, rowp, row & 7, p.scale_log2, -m_run, lim);
       } else {
         ls = masked ? pf_emit<true, BN, T>(s_addr, sPq, row, p.scale_log2, -m_run, lim)
                     : pf_emit<false, BN, T>(s_addr, sPq, row, p.scale_log2, -m_run, lim);
