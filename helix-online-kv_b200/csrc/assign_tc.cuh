@@ -154,6 +154,47 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
 }
 
 constexpr int TC_PRODUCERS = 64;      // threads (two warps) filling A tiles
+
+// The SD values of one row as fp32: 16-byte loads when the row start is
+// 16-byte aligned and SD fills whole loads, element loads otherwise.
+template <int SD>
+__device__ __forceinline__ void tc_load_row(const void* x, int dtype, int64_t base, float (&xv)[SD]) {
+  if (dtype == HOKV_F32) {
+    const float* px = reinterpret_cast<const float*>(x) + base;
+    if (SD % 4 == 0 && (reinterpret_cast<uintptr_t>(px) & 15) == 0) {
+#pragma unroll
+      for (int d = 0; d < SD; d += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(px + d);
+        xv[d] = v.x; xv[d + 1] = v.y; xv[d + 2] = v.z; xv[d + 3] = v.w;
+      }
+      return;
+    }
+  } else {
+    const uint16_t* px = reinterpret_cast<const uint16_t*>(x) + base;
+    if (SD % 8 == 0 && (reinterpret_cast<uintptr_t>(px) & 15) == 0) {
+#pragma unroll
+      for (int d = 0; d < SD; d += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(px + d);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (dtype == HOKV_BF16) {
+            xv[d + 2 * e] = __uint_as_float(w[e] << 16);
+            xv[d + 2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+          } else {
+            const __half2 hh = *reinterpret_cast<const __half2*>(&w[e]);
+            const float2 f = __half22float2(hh);
+            xv[d + 2 * e] = f.x;
+            xv[d + 2 * e + 1] = f.y;
+          }
+        }
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int d = 0; d < SD; ++d) xv[d] = load_as_f32(x, dtype, base + d);
+}
 constexpr int TC_CTA = TC_ROWS + TC_PRODUCERS + 32;   // 4 epilogue warps, 2 producer warps, 1 MMA warp
 
 // Tile geometry of k_pq_assign_tc: K slices of x (KX), B and A row lengths,
@@ -303,7 +344,7 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
       const float* side = reinterpret_cast<const float*>(ring + st * (A_BYTES + SIDE_BYTES) + A_BYTES);
       float xv[SD];
 #pragma unroll
-      for (int d = 0; d < SD; ++d) xv[d] = side[tid * SD + d];
+      for (int d = 0; d < SD; ++d) xv[d] = side[d * TC_ROWS + tid];
       const float x2 = side[TC_ROWS * SD + tid], xa = side[TC_ROWS * (SD + 1) + tid];
       const uint32_t col0 = lane_base + (uint32_t)(a * 128);
       float cmaxs[8];
@@ -389,21 +430,34 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
         const bool valid = i < n;
         const int64_t base = (int64_t)set * xss + (valid ? i : 0) * xrs + (int64_t)s * SD;
         float xv[SD];
+        if (valid) tc_load_row<SD>(x, dtype, base, xv);
+        else {
 #pragma unroll
-        for (int d = 0; d < SD; ++d) xv[d] = valid ? load_as_f32(x, dtype, base + d) : 0.f;
+          for (int d = 0; d < SD; ++d) xv[d] = 0.f;
+        }
         float xa = 0.f;
 #pragma unroll
-        for (int d = 0; d < KL; ++d) {
-          const float v = d < SD ? xv[d] : 0.f;
-          const float hi = split ? tf32_round(v) : v;
-          *reinterpret_cast<float*>(A + cm_off(r, d, KA)) = hi;
-          if (split) *reinterpret_cast<float*>(A + cm_off(r, KL + 8 + d, KA)) = v - hi;
-          xa += fabsf(v);
+        for (int d = 0; d < SD; ++d) xa += fabsf(xv[d]);
+        // 16-byte stores: four consecutive K elements of a row are one
+        // core-matrix row slice (conflict-free across the warp's rows)
+#pragma unroll
+        for (int d4 = 0; d4 < KL / 4; ++d4) {
+          float hv[4], lv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = d4 * 4 + e;
+            const float v = d < SD ? xv[d] : 0.f;
+            hv[e] = split ? tf32_round(v) : v;
+            lv[e] = v - hv[e];
+          }
+          *reinterpret_cast<float4*>(A + cm_off(r, d4 * 4, KA)) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+          if (split)
+            *reinterpret_cast<float4*>(A + cm_off(r, KL + 8 + d4 * 4, KA)) = make_float4(lv[0], lv[1], lv[2], lv[3]);
         }
+        *reinterpret_cast<float4*>(A + cm_off(r, KL, KA)) = make_float4(1.f, 1.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(A + cm_off(r, KL + 4, KA)) = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int d = 0; d < 8; ++d) *reinterpret_cast<float*>(A + cm_off(r, KL + d, KA)) = d < 2 ? 1.f : 0.f;
-#pragma unroll
-        for (int d = 0; d < SD; ++d) side[r * SD + d] = xv[d];
+        for (int d = 0; d < SD; ++d) side[d * TC_ROWS + r] = xv[d];   // [dim][row]: conflict-free
         side[TC_ROWS * SD + r] = sum_sq(xv, SD);
         side[TC_ROWS * (SD + 1) + r] = xa;
       }
