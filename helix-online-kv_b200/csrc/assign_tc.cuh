@@ -195,7 +195,7 @@ __device__ __forceinline__ void tc_load_row(const void* x, int dtype, int64_t ba
 #pragma unroll
   for (int d = 0; d < SD; ++d) xv[d] = load_as_f32(x, dtype, base + d);
 }
-constexpr int TC_CTA = TC_ROWS + TC_PRODUCERS + 32;   // 4 epilogue warps, 2 producer warps, 1 MMA warp
+constexpr int TC_CTA = 2 * TC_ROWS + TC_PRODUCERS + 32;   // 2 x 4 epilogue warps, 2 producer warps, 1 MMA warp
 
 // Tile geometry of k_pq_assign_tc: K slices of x (KX), B and A row lengths,
 // and the A ring depth that keeps two CTAs per SM where it can (at most 113 KB
@@ -209,7 +209,8 @@ struct TcGeo {
   static constexpr int KA = SPLIT ? 2 * KL + 8 : KL + 8;
   static constexpr int A_BYTES = TC_ROWS * KA * 4;
   static constexpr int SIDE_BYTES = TC_ROWS * (SD + 2) * 4;
-  static constexpr int FIXED = 256 * KE * 4 + 256 * KL * 4 + 256 * 4 + 256;
+  static constexpr int XCH = 8 * TC_ROWS * 4;   // the epilogue groups' exchange rows
+  static constexpr int FIXED = 256 * KE * 4 + 256 * KL * 4 + 256 * 4 + XCH + 256;
   static constexpr int PER = A_BYTES + SIDE_BYTES;
   static constexpr int S2 = (113 * 1024 - FIXED) / PER;
   static constexpr int S1 = (227 * 1024 - FIXED) / PER;
@@ -219,21 +220,26 @@ struct TcGeo {
 
 // grid (CTAs), TC_CTA threads; CTA c takes (set, subspace) pair c % pairs and
 // tile group c / pairs.  Roles:
-//   warps 0-3  epilogue: thread r owns row r of a tile (TMEM lane r);
+//   warps 0-3, 7-10  two epilogue groups: thread r of a group owns row r of
+//              a tile (TMEM lane r); group g takes the tiles of accumulator
+//              stage g, so two tiles' epilogues run at once (with a single
+//              256-column stage, group 0 takes every tile);
 //   warps 4-5  producers: x rows of the next tiles into a TC_STAGES ring of
 //              A tiles (x_hi, [1, 1, 0..], x_lo in core-matrix layout) plus
 //              the fp32 row, |x|^2 and |x|_1 the epilogue needs;
 //   warp 6     lane 0 issues the MMAs of a tile into one of the accumulator
 //              stages (two of 128 columns, or one of 256 when more than 128
 //              centroids are live) and commits them to that stage's mbarrier.
-// mbarriers: a_full[s] (64 producer arrivals), a_empty[s] (4 epilogue warps),
-// acc_full[a] (the commit), acc_empty[a] (4 epilogue warps).  Every wait is
+// mbarriers: a_full[s] (64 producer arrivals), a_empty[s] (the 4 warps of the
+// epilogue group that took the tile), acc_full[a] (the commit), acc_empty[a]
+// (4 epilogue warps).  Every wait is
 // bounded; a wait that gives up sets HOKV_ERR_TIMEOUT and the CTA drains.
-// Shared memory: B_hi [256][KE], B_lo [256][KL], |c|^2 [256], then per stage
+// Shared memory: B_hi [256][KE], B_lo [256][KL], |c|^2 [256], the exchange
+// rows of the two epilogue groups [8][128], then per stage
 // A [128][KA] and the rows [128][SD] + |x|^2 [128] + |x|_1 [128], then the
 // barriers and control words.
 template <int SD, bool SPLIT>
-__global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restrict__ x, int dtype, int64_t n, int64_t xrs,
+__global__ void __launch_bounds__(TC_CTA, TcGeo<SD, SPLIT>::S2 >= 2 ? 2 : 1) k_pq_assign_tc(const void* __restrict__ x, int dtype, int64_t n, int64_t xrs,
                                                           int64_t xss, const float* __restrict__ cents, int slots,
                                                           int64_t css, const int* __restrict__ kk, int64_t kss,
                                                           uint8_t* __restrict__ out, int64_t ors, int64_t oss, int M,
@@ -246,7 +252,8 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
   unsigned char* sBh = tc_smem;                                  // 256 x KE
   unsigned char* sBl = sBh + 256 * KE * 4;                       // 256 x KL
   float* csq = reinterpret_cast<float*>(sBl + 256 * KL * 4);     // [256]
-  unsigned char* ring = reinterpret_cast<unsigned char*>(csq + 256);   // TC_STAGES x (A, side)
+  float* xch = csq + 256;                                        // [8][TC_ROWS] epilogue exchange
+  unsigned char* ring = reinterpret_cast<unsigned char*>(xch + 8 * TC_ROWS);   // TC_STAGES x (A, side)
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + TC_STAGES * (A_BYTES + SIDE_BYTES));
   uint64_t* a_full = bars;
   uint64_t* a_empty = bars + TC_STAGES;
@@ -277,11 +284,11 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
   if (tid == 0) {
     for (int i = 0; i < TC_STAGES; ++i) {
       mbar_init(&a_full[i], TC_PRODUCERS);
-      mbar_init(&a_empty[i], 4);
+      mbar_init(&a_empty[i], n_acc == 1 ? 8 : 4);   // both epilogue groups take every tile with one stage
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], n_acc == 1 ? 8 : 4);
     }
     ctl[1] = 0u;
     ctl[2] = 0u;
@@ -327,32 +334,50 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
   volatile uint32_t* abort_flag = &ctl[3];
   auto give_up = [&]() { if (atomicExch(const_cast<uint32_t*>(abort_flag), 1u) == 0u) dev_flag(HOKV_ERR_TIMEOUT); };
 
-  if (warp < 4) {
-    // ---- epilogue: one row per thread ----------------------------------------
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  if (warp < 4 || warp >= 7) {
+    // ---- epilogue: one row per thread (TMEM lane).  With two accumulator
+    //      stages (up to 128 live centroids) group g (warps 0-3 / 7-10) takes
+    //      the tiles of stage g; with one 256-column stage both groups take
+    //      every tile, group g its columns [128 g, 128 g + 128), and they
+    //      combine the row maximum, the candidate counts and the best
+    //      candidate through shared memory at a named barrier (id 1) ----------
+    const int g = warp < 4 ? 0 : 1, quad = warp & 3, r = quad * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     constexpr float N_TERMS = 3 * KL + 2;
     const int nch = np >> 5;
+    const bool halves = n_acc == 1;                         // column split between the groups
+    const int c_lo = halves ? g * 4 : 0, c_hi = halves ? min(nch, g * 4 + 4) : nch;
+    float* xm = xch;                                        // [2][TC_ROWS] half maxima
+    int* xt = reinterpret_cast<int*>(xch + 2 * TC_ROWS);    // [2][TC_ROWS] candidate counts
+    float* xd = xch + 4 * TC_ROWS;                          // [2][TC_ROWS] best distances
+    int* xj = reinterpret_cast<int*>(xch + 6 * TC_ROWS);    // [2][TC_ROWS] best slots
+    auto pair_sync = [&]() { asm volatile("bar.sync 1, 256;" ::: "memory"); };
     int64_t it = 0;
     for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
       const int st = (int)(it % TC_STAGES), a = (int)(it % n_acc);
+      if (!halves && a != g) continue;   // the other group's tile
       const unsigned ph_a = (unsigned)((it / n_acc) & 1);
-      if (*abort_flag || !mbar_wait(&a_full[st], (unsigned)((it / TC_STAGES) & 1)) || !mbar_wait(&acc_full[a], ph_a)) {
+      bool ok = !*abort_flag && mbar_wait(&a_full[st], (unsigned)((it / TC_STAGES) & 1)) && mbar_wait(&acc_full[a], ph_a);
+      if (halves) {   // both groups leave together (the named barriers below need all 8 warps)
+        uint32_t r_ok;
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.and.pred q, 1, 256, p;\n\t"
+                     "selp.u32 %0, 1, 0, q;\n\t}\n" : "=r"(r_ok) : "r"((uint32_t)ok) : "memory");
+        ok = r_ok != 0;
+      }
+      if (!ok) {
         give_up();
         break;
       }
       tc_fence_after();
       const float* side = reinterpret_cast<const float*>(ring + st * (A_BYTES + SIDE_BYTES) + A_BYTES);
-      float xv[SD];
-#pragma unroll
-      for (int d = 0; d < SD; ++d) xv[d] = side[d * TC_ROWS + tid];
-      const float x2 = side[TC_ROWS * SD + tid], xa = side[TC_ROWS * (SD + 1) + tid];
+      const float x2 = side[TC_ROWS * SD + r], xa = side[TC_ROWS * (SD + 1) + r];
       const uint32_t col0 = lane_base + (uint32_t)(a * 128);
       float cmaxs[8];
       float m = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         cmaxs[c] = -INFINITY;
-        if (c < nch) {
+        if (c >= c_lo && c < c_hi) {
           float v[32];
           tmem_ld32(col0 + c * 32, v);
 #pragma unroll
@@ -363,6 +388,11 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
           m = fmaxf(m, cmaxs[c]);
         }
       }
+      if (halves) {
+        xm[g * TC_ROWS + r] = m;
+        pair_sync();
+        m = fmaxf(m, xm[(1 - g) * TC_ROWS + r]);
+      }
       const float e_tc = (N_TERMS + 2.f) * 0x1p-22f * (3.f * xa * cmax + csqmax);
       const float e_ex = 0x1p-22f * ((float)(SD + 1) * xa * cmax + x2 + csqmax);
       const float thr = m - 1.25f * (e_ex + 2.f * e_tc);
@@ -372,7 +402,7 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         cmask[c] = 0u;
-        const bool need = c < nch && cmaxs[c] >= thr;
+        const bool need = c >= c_lo && c < c_hi && cmaxs[c] >= thr;
         if (__any_sync(0xffffffffu, need)) {
           float v[32];
           tmem_ld32(col0 + c * 32, v);
@@ -385,7 +415,13 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
           }
         }
       }
-      // one candidate is the minimiser; several are rescored exactly, in slot order
+      if (halves) {
+        xt[g * TC_ROWS + r] = total;
+        pair_sync();
+        total += xt[(1 - g) * TC_ROWS + r];
+      }
+      // one candidate is the minimiser; several are rescored exactly, in slot
+      // order (the row read back from shared memory)
       float best = INFINITY;
       int bj = 0x7fffffff;
 #pragma unroll
@@ -398,17 +434,25 @@ __global__ void __launch_bounds__(TC_CTA, 1) k_pq_assign_tc(const void* __restri
           for (int d = 0; d < SD; ++d) {
             const float cd = *reinterpret_cast<const float*>(sBh + cm_off(j, d, KE)) +
                              *reinterpret_cast<const float*>(sBl + cm_off(j, d, KL));   // c_hi + c_lo = c
-            acc = ffma(xv[d], cd, acc);
+            acc = ffma(side[d * TC_ROWS + r], cd, acc);
           }
           const float dd = l2_expansion(x2, acc, csq[j]);
           if (dd < best || bj == 0x7fffffff) { best = dd; bj = j; }
         }
       }
-      const int64_t i = tile * TC_ROWS + tid;
-      if (i < n) out[(int64_t)set * oss + i * ors + s] = (uint8_t)(bj == 0x7fffffff ? 0 : bj);
+      if (halves) {   // group 1's slots are all above group 0's: ties keep group 0's
+        xd[g * TC_ROWS + r] = best;
+        xj[g * TC_ROWS + r] = bj;
+        pair_sync();
+        const float ob = xd[(1 - g) * TC_ROWS + r];
+        const int oj = xj[(1 - g) * TC_ROWS + r];
+        if (g == 0 && oj != 0x7fffffff && (bj == 0x7fffffff || ob < best)) bj = oj;
+      }
+      const int64_t i = tile * TC_ROWS + r;
+      if ((!halves || g == 0) && i < n) out[(int64_t)set * oss + i * ors + s] = (uint8_t)(bj == 0x7fffffff ? 0 : bj);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
+      if (lane == 0) {   // 4 arrivals per group that took the tile
         mbar_arrive(&acc_empty[a]);
         mbar_arrive(&a_empty[st]);
       }
