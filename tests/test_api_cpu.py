@@ -150,3 +150,34 @@ def test_cdc03_context_limit_is_refused():
     a.capacity = 248 * 2048 + 256 + 16
     st = lib.hokv_cdc03_workspace_size(ctypes.byref(a), ctypes.byref(need))
     assert st != 0 and b"chunks" in lib.hokv_last_error()
+
+
+def test_prefill_host_checks():
+    """hokv_prefill_attention validates on the host: unsupported dtypes and head
+    dims, causal calls with fewer keys than queries, strides that are not
+    multiples of 8 elements; the Python side accepts only nesting strides and
+    CUDA tensors (no CPU path)."""
+    import torch
+    from helix_online_kv.prefill import _nests, supported
+    L = _lib.lib()
+    args = [None] * 4
+    strides = [0] * 12
+    st = L.hokv_prefill_attention(*args, _lib.F16, 1, 4, 2, 16, 16, 64, *strides, 0.125, 1, None)
+    assert st == _lib.ERR_INVALID and b"null" in L.hokv_last_error()
+    p = ctypes.c_void_p(16)   # never dereferenced: validation fails first
+    st = L.hokv_prefill_attention(p, p, p, p, _lib.F32, 1, 4, 2, 16, 16, 64, *strides, 0.125, 1, None)
+    assert st == _lib.ERR_UNSUPPORTED and b"dtype" in L.hokv_last_error()
+    st = L.hokv_prefill_attention(p, p, p, p, _lib.BF16, 1, 4, 2, 16, 16, 96, *strides, 0.125, 1, None)
+    assert st == _lib.ERR_UNSUPPORTED and b"head_dim" in L.hokv_last_error()
+    st = L.hokv_prefill_attention(p, p, p, p, _lib.BF16, 1, 4, 2, 32, 16, 64, *strides, 0.125, 1, None)
+    assert st == _lib.ERR_INVALID and b"kv_len >= q_len" in L.hokv_last_error()
+    bad = [8] * 12
+    bad[2] = 12
+    st = L.hokv_prefill_attention(p, p, p, p, _lib.BF16, 1, 4, 2, 16, 16, 64, *bad, 0.125, 1, None)
+    assert st == _lib.ERR_INVALID and b"stride" in L.hokv_last_error()
+    # stride nesting (the tensor maps' requirement), checked on CPU tensors
+    assert _nests(torch.empty(2, 600, 8, 64).transpose(1, 2))            # a model's transposed projection
+    assert _nests(torch.empty(2, 2, 2048, 64)[:, :, :600])               # a store slice
+    assert not _nests(torch.as_strided(torch.empty(4096), (1, 2, 16, 64), (4096, 64, 64, 1)))   # aliasing
+    q = torch.zeros(1, 2, 16, 64, dtype=torch.float16)
+    assert not supported(q, q, q)                                        # CPU tensors: no kernel, no fallback
