@@ -398,8 +398,9 @@ def head_sharded(world, rank, steps, S=16384, Ls=31):
     31 layers, its KV heads split over the ranks; after every layer one
     all-gather of the [1, 32, 128] outputs over NCCL, whose result is the next
     layer's queries (a stand-in for the model's projections), so that each
-    layer waits for the collective.  Eager launches, device-timed, max over
-    ranks."""
+    layer waits for the collective.  The step (decodes and collectives) is
+    captured in a CUDA graph where the collective library allows it, else
+    launched eagerly (the line names which); device-timed, max over ranks."""
     import torch
     from helix_online_kv.cdc03 import CDC03Store
     from helix_online_kv.sharding import gather_heads, head_shard, max_over_ranks
