@@ -193,46 +193,39 @@ struct QuantScale {
   float inv;
   int margin;
 };
-__device__ __forceinline__ QuantScale quant_scale(const float* lo, const float* hi, int M, float scale) {
-  const int qmax = qmax_for(M);
-  float rmax = 0.f;
-  double sa = 0.0;
-  for (int s = 0; s < M; ++s) {
-    rmax = fmaxf(rmax, hi[s] - lo[s]);
-    sa += fmax(fabs((double)lo[s]), fabs((double)hi[s]));
-  }
-  const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
-  const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
-  const bool ok_scale = (scale > 0.f) && isfinite(scale) && isfinite(sa);
-  QuantScale r;
-  r.inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
-  r.margin = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
-  return r;
-}
-
-// quant_scale computed by one warp: lane s takes subspace s (and s + 32), the
-// largest range and the sum of max(|lo|, |hi|) are warp reductions.  Every
-// lane returns the result.
+// The step and band computed by one warp: lane s takes subspace s (and
+// s + 32); the largest range and the sum sa of max(|lo|, |hi|) are warp
+// reductions.  The band is
+//   margin = ceil(M * 1.0002 + (M + 1) 2^-22 sa / delta),  delta = rmax / qmax,
+// evaluated in fp32 with every rounding pushed upward (sa, the quotient and
+// the sum each scaled by 1 + 2^-20, more than the relative error of the
+// at most 7 fp32 additions and 4 products and quotients behind them), so the
+// margin is never below the exact value of the formula; at worst it is one
+// code unit wider, which admits a few more candidates and changes no
+// selection.  A band past 2^30, or a scale that cannot rank, gives 2^30.
+// Every lane returns the result.
 __device__ __forceinline__ QuantScale quant_scale_warp(const float* lo, const float* hi, int M, float scale,
                                                        int lane) {
   const int qmax = qmax_for(M);
-  float rmax = 0.f;
-  double sa = 0.0;
+  float rmax = 0.f, sa = 0.f;
   for (int s = lane; s < M; s += 32) {
     rmax = fmaxf(rmax, hi[s] - lo[s]);
-    sa += fmax(fabs((double)lo[s]), fabs((double)hi[s]));
+    sa += fmaxf(fabsf(lo[s]), fabsf(hi[s]));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
     sa += __shfl_xor_sync(0xffffffffu, sa, o);
   }
-  const double delta = rmax > 0.f ? (double)rmax / qmax : 1.0;
-  const double e_f = (double)(M + 1) * ldexp(1.0, -22) * sa / delta;
-  const bool ok_scale = (scale > 0.f) && isfinite(scale) && isfinite(sa);
+  constexpr float UP = 1.f + 0x1p-20f;
+  const float sa_up = sa * UP;
+  float e_f = (float)(M + 1) * 0x1p-22f * sa_up;
+  if (rmax > 0.f) e_f = e_f * (float)qmax / rmax * UP;   // / delta
+  const float band = ((float)M * 1.0002f + e_f) * UP;
+  const bool ok_scale = (scale > 0.f) && isfinite(scale) && isfinite(sa) && band < 1.0e9f;
   QuantScale r;
   r.inv = rmax > 0.f ? (float)qmax / rmax : 0.f;
-  r.margin = ok_scale ? (int)ceil((double)M * 1.0002 + e_f) : (1 << 30);
+  r.margin = ok_scale ? (int)ceilf(band) : (1 << 30);
   return r;
 }
 
@@ -512,12 +505,19 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       default: dev_flag(HOKV_ERR_DEVICE_INPUT);
     }
     // this CTA's codes into L2 while the cluster exchanges and quantises the
-    // tables (issued after the table reads, which are on the critical path)
-    for (int i = 0; i < n_mine; ++i) {
-      const int t0 = (me + i * R) * K6_CHUNK;
-      const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
-      for (int64_t off = (int64_t)tid * 128; off < nbytes; off += (int64_t)K6_THREADS * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(gcodes + (int64_t)t0 * CS + off));
+    // tables (issued after the table reads, which are on the critical path):
+    // one bulk prefetch per chunk from one thread, so the load/store pipe
+    // stays free for the phases that follow (the 16-byte-aligned interior of
+    // each chunk; a prefetch is only a hint)
+    if (tid == 0) {
+      for (int i = 0; i < n_mine; ++i) {
+        const int t0 = (me + i * R) * K6_CHUNK;
+        const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
+        const uintptr_t a0 = reinterpret_cast<uintptr_t>(gcodes + (int64_t)t0 * CS);
+        const uintptr_t lo = (a0 + 15) & ~(uintptr_t)15, hi = (a0 + (uintptr_t)nbytes) & ~(uintptr_t)15;
+        if (hi > lo)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
+      }
     }
     __syncthreads();
     stamp(0, scta, 2);   // dots done
@@ -547,6 +547,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       }
     }
     __syncthreads();
+    stamp(0, scta, 4);   // quantisation step known
     unsigned char* gimg = p.qimg + (int64_t)u * p.qimg_bytes;
     {
       const int qmax = qmax_for(M), j = tid;
@@ -576,7 +577,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
         if (own == me) put_entry<CS, GT>(gimg, sx, j, code);
       }
     }
-    stamp(0, scta, 4);   // own image entries written
+    stamp(0, scta, 5);   // own image entries written
     cluster_arrive();           // phase C: the image is complete in memory
 #pragma unroll
     for (int it = 0; it < HT; ++it) {   // first codes of the first chunk meanwhile
@@ -588,11 +589,11 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       }
     }
     cluster_wait();
-    stamp(0, scta, 5);   // every CTA's image entries written
+    stamp(0, scta, 6);   // every CTA's image entries written
     for (int i = tid; i < Q::BYTES / 16; i += K6_THREADS) cp_async16(qlut + i * 16, gimg + (int64_t)i * 16);
     cp_async_wait_all();
     __syncthreads();
-    stamp(0, scta, 6);   // image in shared memory
+    stamp(0, scta, 7);   // image in shared memory
   }
 
   // ---- quantised scores of one chunk, kept in registers ----------------------
@@ -754,9 +755,9 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
 
   // ---- histograms of every own chunk, pooled; threshold ----------------------
   for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
-  stamp(0, scta, 7);   // own chunks scored (thread 0)
+  stamp(0, scta, 8);   // own chunks scored (thread 0)
   pool_cluster<GT * HWORDS>(hist, full, R, me);
-  stamp(0, scta, 8);   // histograms pooled
+  stamp(0, scta, 9);   // histograms pooled
   if (warp < GT) {
     const int g = warp;
     const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
@@ -764,7 +765,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
       s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
   __syncthreads();
-  stamp(0, scta, 9);   // threshold known
+  stamp(0, scta, 10);   // threshold known
 
   // ---- candidates: the last scored chunk from registers, the others scored again
   emit_chunk(me + (n_mine - 1) * R);
@@ -772,7 +773,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     score_chunk(me + i * R, false, false);
     emit_chunk(me + i * R);
   }
-  stamp(0, scta, 10);  // candidates listed and rescored
+  stamp(0, scta, 11);  // candidates listed and rescored
 }
 
 template <int D, typename KVT>
