@@ -351,6 +351,11 @@ __global__ void __launch_bounds__(256) k_pq_assign_seq(const void* __restrict__ 
     bj[v] = 0x7fffffff;
   }
   __syncthreads();
+  if (i0 >= n) return;   // no vector of this thread in range (small batches): nothing to score
+  // vectors v < nv of this block's threads can be in range (the same for the
+  // whole block, so the branch below does not diverge)
+  const int64_t left = n - (int64_t)blockIdx.x * 256 * V;
+  const int nv = left >= 256 * V ? V : (int)((left + 255) / 256);
   for (int j = 0; j < k; ++j) {
     float c[SD];
 #pragma unroll
@@ -358,6 +363,7 @@ __global__ void __launch_bounds__(256) k_pq_assign_seq(const void* __restrict__ 
     const float cj2 = c2[j];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
+      if (v >= nv) break;
       float acc = 0.f;
 #pragma unroll
       for (int d = 0; d < SD; ++d) acc = ffma(xv[v][d], c[d], acc);

@@ -443,8 +443,10 @@ int hokv_pq_assign(const void* x, int x_dtype, int64_t n, int64_t x_row_stride, 
                                     S(stream));
     if (st != -1) return st;
   }
-  if (dot_order == DOT_SEQ_FMA && (sub_dim == 4 || sub_dim == 8)) {
-    // prefill-sized batches: register-tiled kernel, same arithmetic
+  if (dot_order == DOT_SEQ_FMA && (sub_dim == 4 || sub_dim == 8) && n >= 64) {
+    // mid-sized batches: register-tiled kernel, same arithmetic (below 64
+    // rows most of its threads would have no row; the warp-per-vector kernel
+    // below splits the centroids over the lanes instead)
     HOKV_REQUIRE(cdiv(n, 1024) < (1ll << 31) && M <= 65535 && n_sets <= 65535, "pq_assign: grid too large");
     const dim3 grid((unsigned)cdiv(n, 1024), (unsigned)M, (unsigned)n_sets);
 #define HOKV_PQA(sd_, v_)                                                                                          \
