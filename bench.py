@@ -556,6 +556,38 @@ def tinyllama_generate(prompt=1024, new=256, seed=0):
     return res
 
 
+def path_a_sweep(reps=20):
+    """Path A, the fused Q.K^T over scalar-VQ codes (fused_scalar_vq_qkt, the
+    reference's Triton kernel triton_attention.py:25-66 restated as
+    hokv_scalar_vq_qkt): one head_dim-128 query against S tokens of uint8
+    codes and a 256-entry fp32 codebook, fp32 accumulation.  Device time per
+    call (back-to-back calls after a warm-up) and the index bytes read per
+    second; at 1M tokens the 128 MB of codes exceed L2."""
+    import torch
+    from helix_online_kv.triton_attention import fused_scalar_vq_qkt
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(21)
+    D = 128
+    q = torch.randn(D, generator=gen, device="cuda")
+    cb = torch.randn(256, generator=gen, device="cuda")
+    res = {}
+    for S in (16384, 131072, 1048576):
+        idx = torch.randint(0, 256, (S, D), generator=gen, device="cuda", dtype=torch.int32).to(torch.uint8)
+        fused_scalar_vq_qkt(q, idx, cb, 0.088)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fused_scalar_vq_qkt(q, idx, cb, 0.088)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        nbytes = S * D + S * 4   # codes in, scores out
+        res[f"S_{S}"] = {"us": ms * 1e3, "gbs": nbytes / (ms * 1e-3) / 1e9}
+        del idx
+    return res
+
+
 def prefill_attention_sweep(reps=10):
     """Exact causal prefill attention of one layer (hokv_prefill_attention)
     beside torch's SDPA on the same tensors: a 1024-token TinyLlama prompt
@@ -888,7 +920,8 @@ def run_ours(args):
                          ("long_context", lambda: long_context(world, rank, max(3, min(args.steps, 10)))),
                          ("head_sharded_1seq", lambda: head_sharded(world, rank, max(3, min(args.steps, 10)))),
                          ("tinyllama_generate", lambda: tinyllama_generate() if world == 1 else {"skipped": "1 GPU only"}),
-                         ("prefill_attention", lambda: prefill_attention_sweep() if world == 1 else {"skipped": "1 GPU only"})):
+                         ("prefill_attention", lambda: prefill_attention_sweep() if world == 1 else {"skipped": "1 GPU only"}),
+                         ("path_a_scalar_vq_qkt", lambda: path_a_sweep() if world == 1 else {"skipped": "1 GPU only"})):
             try:
                 extras[name] = fn()
             except Exception as e:   # noqa: BLE001 - reported in the line

@@ -1341,4 +1341,46 @@ __global__ void __launch_bounds__(256) k_scalar_vq_qkt(const float* __restrict__
   scores[t] = (float)(acc * (ACC)scale);
 }
 
+// The same for uint8 codes with head_dim = 16 * LPT (LPT = 1..32 lanes per
+// token) and 16-byte-aligned rows: LPT lanes share a token, each loads 16
+// codes with one 16-byte load (a warp reads 32 / LPT whole rows, contiguous
+// when the rows are), looks them up in the lane-replicated codebook (bank of
+// lane L = L: conflict-free for any code) and multiplies by its 16 query
+// values kept in registers; the LPT partial sums are added by shuffles.  A
+// grid-stride loop, so each CTA fills the replicated codebook once.
+template <int LPT, typename ACC>
+__global__ void __launch_bounds__(256) k_scalar_vq_qkt_u8v(const float* __restrict__ q, const uint8_t* __restrict__ idx,
+                                                           int64_t S, int64_t stride, const float* __restrict__ cbk,
+                                                           int k, float scale, float* __restrict__ scores) {
+  __shared__ float rep[256 * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+    const int j = i >> 5;
+    rep[i] = (j < k) ? cbk[j] : 0.f;
+  }
+  const int sub = lane % LPT;   // this lane's 16 dims: [16 sub, 16 sub + 16)
+  float qv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) qv[i] = q[sub * 16 + i];
+  __syncthreads();
+  constexpr int TPW = 32 / LPT;   // tokens per warp and step
+  const int64_t step = (int64_t)gridDim.x * 8 * TPW;
+  for (int64_t t0 = ((int64_t)blockIdx.x * 8 + warp) * TPW; t0 < S; t0 += step) {
+    const int64_t t = t0 + lane / LPT;
+    ACC acc = 0;
+    if (t < S) {
+      const uint4 w = *reinterpret_cast<const uint4*>(idx + t * stride + sub * 16);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = (int)((ws[i >> 2] >> (8 * (i & 3))) & 0xffu);
+        acc += (ACC)qv[i] * (ACC)rep[j * 32 + lane];
+      }
+    }
+#pragma unroll
+    for (int o = LPT / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (sub == 0 && t < S) scores[t] = (float)(acc * (ACC)scale);
+  }
+}
+
 }  // namespace hokv

@@ -288,6 +288,28 @@ int hokv_scalar_vq_qkt(const float* q, const void* idx, int idx_dtype, int64_t s
   HOKV_REQUIRE(k >= 1 && k <= 256, "scalar_vq_qkt: k=%d", k);
   HOKV_REQUIRE(idx_dtype == HOKV_U8 || idx_dtype == HOKV_I32, "scalar_vq_qkt: idx dtype %d", idx_dtype);
   if (seq_len == 0) return HOKV_OK;
+  if (idx_dtype == HOKV_U8 && head_dim % 16 == 0 && (head_dim / 16) <= 32 && ((head_dim / 16) & (head_dim / 16 - 1)) == 0 &&
+      idx_stride % 16 == 0 && aligned(idx, 16)) {
+    // coalesced 16-byte code loads, lanes of a token combined by shuffles
+    int dev = 0, n_sm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const int lpt = head_dim / 16;
+    const int64_t per_cta = 8 * (32 / lpt);   // warps x tokens per step
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(cdiv(seq_len, per_cta), (int64_t)n_sm * 6));
+#define HOKV_QKT(L_)                                                                                              \
+  if (lpt == L_) {                                                                                              \
+    if (accum_f64)                                                                                              \
+      k_scalar_vq_qkt_u8v<L_, double><<<grid, 256, 0, S(stream)>>>(q, (const uint8_t*)idx, seq_len, idx_stride,  \
+                                                                    codebook, k, scale, scores);                \
+    else                                                                                                        \
+      k_scalar_vq_qkt_u8v<L_, float><<<grid, 256, 0, S(stream)>>>(q, (const uint8_t*)idx, seq_len, idx_stride,   \
+                                                                   codebook, k, scale, scores);                 \
+    return check_launch("k_scalar_vq_qkt_u8v");                                                                 \
+  }
+    HOKV_QKT(1) HOKV_QKT(2) HOKV_QKT(4) HOKV_QKT(8) HOKV_QKT(16) HOKV_QKT(32)
+#undef HOKV_QKT
+  }
   const unsigned grid = (unsigned)cdiv(seq_len, 256);
   const size_t sm = (size_t)head_dim * 4;
   if (idx_dtype == HOKV_U8) {
