@@ -1086,9 +1086,14 @@ def main():
                          "whose JSON line is then not the workload's")
     ap.add_argument("--phase-stamps", action="store_true",
                     help="run one step with the profiling build (libhokv_stamps.so) and print per-phase times")
+    ap.add_argument("--path-a-sweep", action="store_true",
+                    help="only the Path A sweep (fused Q.K^T over scalar-VQ codes), one JSON line")
     ap.add_argument("--prefill-sweep", action="store_true",
                     help="only the prefill-attention sweep (hokv_prefill_attention beside SDPA), one JSON line")
     args = ap.parse_args()
+    if args.path_a_sweep:
+        print(json.dumps({"path_a_scalar_vq_qkt": path_a_sweep()}))
+        return 0
     if args.prefill_sweep:
         print(json.dumps({"prefill_attention": prefill_attention_sweep()}))
         return 0
