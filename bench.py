@@ -997,7 +997,8 @@ def run_ours(args):
 
 K6_PHASES = ["rows+queries staged", "dots", "ranges exchanged", "quantisation step", "own image entries",
              "cluster image barrier",
-             "image to smem", "score own chunks", "pool histograms", "threshold", "list+rescore"]
+             "image to smem", "score own chunks", "histograms complete (cluster barrier)", "threshold",
+             "list+rescore"]
 K7_PHASES = ["hot window", "wait for k6", "selection", "attend selected", "combine+store"]
 
 

@@ -257,54 +257,17 @@ __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
-// Sum the NW-word histograms `hist` of the R CTAs of the cluster into every
-// CTA's `full`: rank r adds up slice r (16-byte reads of distributed shared
-// memory) and stores the sum into the `full` of every rank.  Two cluster
-// barrier phases; afterwards no CTA touches another's shared memory.
-template <int NW>
-__device__ __forceinline__ void pool_cluster(const uint32_t* hist, uint32_t* full, int R, int me) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cl = cg::this_cluster();
-  constexpr int NV = NW / 4;
-  const int per = (NV + R - 1) / R;
-  cluster_arrive();
-  cluster_wait();   // every CTA's histogram is complete
-  for (int i = threadIdx.x; i < per; i += blockDim.x) {
-    const int v = me * per + i;
-    if (v >= NV) break;
-    // each 16-bit counter summed in 32 bits and saturated at 65535: an
-    // undercount only lowers the threshold (more candidates, same selection)
-    uint32_t lo[4] = {0u, 0u, 0u, 0u}, hi[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk) {
-      if (rk < R) {
-        const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(const_cast<uint32_t*>(hist), (unsigned)rk))[v];
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) { lo[k] += xs[k] & 0xffffu; hi[k] += xs[k] >> 16; }
-      }
-    }
-    uint32_t ws[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) ws[k] = min(lo[k], 0xffffu) | (min(hi[k], 0xffffu) << 16);
-    const uint4 acc = make_uint4(ws[0], ws[1], ws[2], ws[3]);
-#pragma unroll
-    for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk)
-      if (rk < R) reinterpret_cast<uint4*>(cl.map_shared_rank(full, (unsigned)rk))[v] = acc;
-  }
-  cluster_arrive();
-  cluster_wait();   // every slice is in every CTA's `full`
-}
-
-// Largest bin b of one head's packed histogram (HWORDS words, bin 2i in the
-// low half of word i) such that at least kp items lie in bins >= b; -1 if
-// the histogram holds fewer than kp items.  One warp; lane L owns bins
-// [32L, 32L + 32).
-__device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane) {
+// Per-lane coarse counts of one CTA's packed histograms: coarse[g * 32 + L] =
+// items of head g in bins [32L, 32L + 32) (words [16L, 16L + 16)).  Threads
+// [0, GT * 32); lane L's 16 words as four 16-byte loads, rotated by lane so
+// that a quarter warp spreads over the bank groups.
+template <int GT>
+__device__ __forceinline__ void coarse_counts(const uint32_t* hist, uint32_t* coarse) {
   static_assert(HWORDS == 512, "32 lanes x 16 words");
-  // lane L's 16 words as four 16-byte loads, rotated by lane so that a quarter
-  // warp spreads over the bank groups
-  const uint4* h4 = reinterpret_cast<const uint4*>(h);
+  const int i = threadIdx.x;
+  if (i >= GT * 32) return;
+  const int g = i >> 5, lane = i & 31;
+  const uint4* h4 = reinterpret_cast<const uint4*>(hist + g * HWORDS);
   uint32_t ls = 0;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -312,6 +275,25 @@ __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane)
     ls += (v.x & 0xffffu) + (v.x >> 16) + (v.y & 0xffffu) + (v.y >> 16) + (v.z & 0xffffu) + (v.z >> 16) +
           (v.w & 0xffffu) + (v.w >> 16);
   }
+  coarse[i] = ls;
+}
+
+// Largest bin b of head g's histogram pooled over the R CTAs of the cluster
+// (HWORDS words per CTA, bin 2i in the low half of word i) such that at least
+// kp items lie in bins >= b; -1 if the cluster holds fewer than kp items.  One
+// warp, reading the other CTAs' shared memory: first the R coarse counts of
+// each lane's 32 bins, then the R copies of the 16 words of the lane range
+// that holds b.  Counts are summed in 32 bits (no saturation).  The caller
+// has made every CTA's `hist` and `coarse` visible (cluster barrier) and
+// keeps them unchanged until every CTA has passed this call (the next).
+__device__ __forceinline__ int top_bin_cluster(const uint32_t* hist_g, const uint32_t* coarse_g, uint32_t kp,
+                                               int lane, int R) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  uint32_t ls = 0;
+#pragma unroll
+  for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk)
+    if (rk < R) ls += cl.map_shared_rank(const_cast<uint32_t*>(coarse_g), (unsigned)rk)[lane];
   uint32_t suf = ls;   // items in lanes >= this one's bins
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -325,8 +307,14 @@ __device__ __forceinline__ int top_bin(const uint32_t* h, uint32_t kp, int lane)
   // low half of word i), and the warp finds the highest j whose suffix count,
   // with the items above the range, still reaches kp
   const uint32_t above = __shfl_sync(0xffffffffu, suf - ls, lstar);
-  const uint32_t w = h[lstar * 16 + (lane >> 1)];
-  uint32_t c = (lane & 1) ? (w >> 16) : (w & 0xffffu);
+  uint32_t c = 0;
+#pragma unroll
+  for (int rk = 0; rk < K6_CLUSTER_MAX; ++rk) {
+    if (rk < R) {
+      const uint32_t w = cl.map_shared_rank(const_cast<uint32_t*>(hist_g), (unsigned)rk)[lstar * 16 + (lane >> 1)];
+      c += (lane & 1) ? (w >> 16) : (w & 0xffffu);
+    }
+  }
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t t = __shfl_down_sync(0xffffffffu, c, o);
@@ -412,7 +400,7 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* qlut = smem;                                              // Q::BYTES
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + Q::BYTES);           // [GT][HWORDS]
-  uint32_t* full = hist + GT * HWORDS;                                     // [GT][HWORDS] pooled
+  uint32_t* coarse = hist + GT * HWORDS;                                   // [GT][32] per-lane counts
   __shared__ int s_margin[GT], s_thr[GT], s_cnt[GT], s_nl[GT];
 
   pdl_launch_dependents();
@@ -756,16 +744,25 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
   // ---- histograms of every own chunk, pooled; threshold ----------------------
   for (int i = 0; i < n_mine; ++i) score_chunk(me + i * R, i == 0, true);
   stamp(0, scta, 8);   // own chunks scored (thread 0)
-  pool_cluster<GT * HWORDS>(hist, full, R, me);
-  stamp(0, scta, 9);   // histograms pooled
+  // the unit-wide threshold straight from every CTA's histograms: per-lane
+  // coarse counts, one cluster barrier, then each head's warp reads the R
+  // coarse counts and the R copies of one 32-bin range through distributed
+  // shared memory
+  __syncthreads();
+  coarse_counts<GT>(hist, coarse);
+  cluster_arrive();
+  cluster_wait();   // every CTA's histograms and coarse counts are complete
+  stamp(0, scta, 9);   // histograms complete in the cluster
   if (warp < GT) {
     const int g = warp;
-    const int bstar = top_bin(full + g * HWORDS, (uint32_t)cr.kp, lane);
+    const int bstar = top_bin_cluster(hist + g * HWORDS, coarse + g * 32, (uint32_t)cr.kp, lane, R);
     if (lane == 0)
       s_thr[g] = (s_margin[g] >= (1 << 30) || bstar < 0) ? -(1 << 30) : (bstar << HSHIFT) - s_margin[g];
   }
+  cluster_arrive();   // this CTA no longer reads the others' histograms
   __syncthreads();
   stamp(0, scta, 10);   // threshold known
+  cluster_wait();     // nor does any other CTA read this one's: the list may reuse them
 
   // ---- candidates: the last scored chunk from registers, the others scored again
   emit_chunk(me + (n_mine - 1) * R);

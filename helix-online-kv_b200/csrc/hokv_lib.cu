@@ -105,7 +105,7 @@ template <int CS, int GT>
 static int launch_stage1(const Cdc03P& p, cudaStream_t st) {
   using Q = QGeo<CS, GT>;
   if (p.chunk != K6_CHUNK) return fail(HOKV_ERR_INVALID, "cdc03: chunk %d != %d", p.chunk, K6_CHUNK);
-  const size_t sm = Q::BYTES + (size_t)2 * GT * HWORDS * 4;   // table image, histograms, pooled histograms
+  const size_t sm = Q::BYTES + (size_t)GT * (HWORDS + 32) * 4;   // table image, histograms, coarse counts
   const int R = std::min(p.n_chunks, K6_CLUSTER_MAX);
   if (int e = ensure_smem(k6_candidates<CS, GT>, sm)) return e;
   return launch_ex(k6_candidates<CS, GT>, dim3((unsigned)R, (unsigned)(p.B * p.Hkv)), dim3(K6_THREADS), sm, st, p,
