@@ -58,6 +58,7 @@ struct Cdc03P {
   float* texact;          // [units][GT][CS][256]    exact sub-tables (K6 rescoring, K7 rescans)
   int* margin;            // [units][GT]             error band in code units
   int n_chunks, chunk, GT, qimg_bytes;
+  int kv_es;              // bytes per K/V element
 };
 
 // Per-sequence geometry of the cold range, identical in all three kernels.
@@ -77,6 +78,23 @@ __device__ __forceinline__ ColdRange cold_range(const Cdc03P& p, int b) {
 }
 
 // ---- async copies and programmatic dependent launch ------------------------
+// Hint: bring the 16-byte-aligned interior of [base + off, base + off + nbytes)
+// into L2 with one bulk prefetch (nothing happens when it is empty).
+__device__ __forceinline__ void prefetch_l2(const void* base, int64_t off, int64_t nbytes) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(base) + (uintptr_t)off;
+  const uintptr_t lo = (a0 + 15) & ~(uintptr_t)15, hi = (a0 + (uintptr_t)nbytes) & ~(uintptr_t)15;
+  if (nbytes > 0 && hi > lo)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
+}
+
+// Hint: the 128-byte lines of [base + off, base + off + nbytes) into L2, one
+// prefetch instruction a line (cheap to issue from many threads; the bulk
+// prefetch above goes through the CTA's asynchronous copy unit, one at a time).
+__device__ __forceinline__ void prefetch_lines_l2(const void* base, int64_t off, int64_t nbytes) {
+  const char* a = static_cast<const char*>(base) + off;
+  for (int64_t o = 0; o < nbytes; o += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(a + o));
+}
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
@@ -500,12 +518,17 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
     if (tid == 0) {
       for (int i = 0; i < n_mine; ++i) {
         const int t0 = (me + i * R) * K6_CHUNK;
-        const int64_t nbytes = (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS;
-        const uintptr_t a0 = reinterpret_cast<uintptr_t>(gcodes + (int64_t)t0 * CS);
-        const uintptr_t lo = (a0 + 15) & ~(uintptr_t)15, hi = (a0 + (uintptr_t)nbytes) & ~(uintptr_t)15;
-        if (hi > lo)
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo)) : "memory");
+        prefetch_l2(gcodes, (int64_t)t0 * CS, (int64_t)max(0, min(t0 + K6_CHUNK, cr.Sc) - t0) * CS);
       }
+    }
+    // the K and V rows k7 reads whatever the selection (the hot window and the
+    // sink tokens) into L2 meanwhile, by the last CTA of the cluster
+    if (tid == 32 && me == R - 1) {
+      const int64_t rb = (int64_t)p.D * p.kv_es, base = ((int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh) * p.kv_es;
+      prefetch_l2(p.k, base + cr.Sc * rb, (int64_t)(cr.S - cr.Sc) * rb);
+      prefetch_l2(p.v, base + cr.Sc * rb, (int64_t)(cr.S - cr.Sc) * rb);
+      prefetch_l2(p.k, base, (int64_t)cr.sink * rb);
+      prefetch_l2(p.v, base, (int64_t)cr.sink * rb);
     }
     __syncthreads();
     stamp(0, scta, 2);   // dots done
@@ -731,6 +754,12 @@ __global__ void __launch_bounds__(K6_THREADS, k6_min_blocks<CS, GT>()) k6_candid
 #pragma unroll
       for (int s = 0; s < CS; ++s) if (s < M) sum = fadd(sum, e[s]);
       keys[g * CAND_MAX + slot] = sel_key(fmul(sum, scale), t);
+      // the candidate's K and V rows into L2 for k7's attention over the
+      // selected tokens (a hint; every head's copy of a token prefetches it)
+      const int64_t rb = (int64_t)p.D * p.kv_es;
+      const int64_t ro = ((int64_t)b * p.kv_sb + (int64_t)h * p.kv_sh) * p.kv_es + (int64_t)t * rb;
+      prefetch_lines_l2(p.k, ro, rb);
+      prefetch_lines_l2(p.v, ro, rb);
     }
     __syncthreads();
     if (tid < GT) {

@@ -659,6 +659,7 @@ static Cdc03P make_params(const hokv_cdc03_args* a, const Plan& pl) {
   p.q = a->q; p.q_dtype = a->q_dtype; p.q_sb = a->q_stride_b;
   p.out = a->out; p.out_dtype = a->out_dtype; p.out_sb = a->out_stride_b;
   p.k = a->k; p.v = a->v; p.kv_sb = a->kv_stride_b; p.kv_sh = a->kv_stride_h; p.cap = a->capacity;
+  p.kv_es = a->kv_dtype == HOKV_F32 ? 4 : 2;
   p.codes = a->codes; p.c_sb = a->code_stride_b; p.c_sh = a->code_stride_h;
   p.cb = a->codebook; p.cb_sb = a->cb_stride_b; p.cb_sh = a->cb_stride_h;
   p.cbk = a->cb_k; p.cbk_sb = a->cbk_stride_b; p.cbk_sh = a->cbk_stride_h;

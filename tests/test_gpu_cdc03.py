@@ -278,9 +278,9 @@ def test_ties_and_candidate_overflow():
 
 def test_one_bin_holding_more_than_65535_tokens():
     """80K identical keys: every score falls in one histogram bin, whose count
-    over the whole cluster passes the 16-bit counters.  The pooled count
-    saturates (the threshold can only drop), every chunk's list overflows and
-    is rescanned exactly, and the selection is the lowest token indices."""
+    over the whole cluster passes the 16-bit counters of one CTA.  The
+    cluster's count is summed in 32 bits, every chunk's list overflows and is
+    rescanned exactly, and the selection is the lowest token indices."""
     from helix_online_kv.cdc03 import CDC03Store
     B, H, S, D, M = 1, 1, 80000, 64, 8
     st = CDC03Store(B, 1, H, D, S, n_subspaces=M, dtype=torch.float16)
