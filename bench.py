@@ -53,17 +53,23 @@ def _peaks():
         return 6650.0, "fallback"
 
 
-def _traffic_from_profiles(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+def _profile_field(kernel: str, field: str):
+    """The `field:` line of `kernel`'s committed ncu summary (text after the colon), if any."""
     path = os.path.join(REPO, "profiles", f"{kernel}_llama3_16k.md")
     try:
         with open(path) as f:
             for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip().split()[0])
+                if line.startswith(field + ":"):
+                    return line.split(":", 1)[1].strip()
     except OSError:
         pass
     return None
+
+
+def _traffic_from_profiles(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+    v = _profile_field(kernel, "traffic_bytes_per_launch")
+    return float(v.split()[0]) if v else None
 
 
 # ----------------------------------------------------------------------------- reference arm (CPU)
@@ -854,6 +860,7 @@ def run_ours(args):
         key = "k7_select_attend" if name.startswith("k7") else "k6_candidates"
         return {"kernel": name, "bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                 "traffic": _traffic_from_profiles(key), "algorithmic_bytes": nbytes, "avg_launch_ms": kms,
+                "traffic_note": _profile_field(key, "traffic_note"),
                 "peak_kind": f"{peak_kind} (hbm_gbs, MEASURED_PEAKS.json)" if peak_kind == "measured" else peak_kind}
 
     step_bytes = (k6_bytes + k7_bytes) * Ls
